@@ -1,0 +1,213 @@
+/*
+ * h3b.h — C ABI of the B200 (sm_100a) kernels behind the MiniMax-H3 DiT-block
+ * hot path.
+ *
+ * Conventions
+ *  - Plain device pointers, int64 sizes/strides in elements, scalars, and an
+ *    explicit cudaStream_t.  No torch types, no exceptions across the ABI.
+ *  - Every entry point returns 0 (H3B_OK) or one of the H3B_ERR_* codes below.
+ *    Shape, alignment and dtype violations are rejected on the host before any
+ *    launch.  Device-side waits are bounded; a wait that times out records
+ *    H3B_ERR_DEVICE_TIMEOUT in a device status word read by
+ *    h3b_device_status().
+ *  - Entry points allocate no device memory and never synchronise the host
+ *    (h3b_device_status() excepted); callers own every buffer.
+ *  - bf16 = IEEE bfloat16 stored as uint16; e4m3 = OCP float8 e4m3fn; e2m1
+ *    codes are 4-bit values packed two per byte.
+ *
+ * Reference paths (repository BHUHD/minixmax-h3) are given relative to
+ * Ref2VA-910C-FastAPI-INT8-CANN9.1.0/runtime/src/h3_npu/.
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define H3B_API __attribute__((visibility("default")))
+#else
+#define H3B_API
+#endif
+
+enum {
+  H3B_OK = 0,
+  H3B_ERR_SHAPE = 1,          /* unsupported or inconsistent sizes          */
+  H3B_ERR_ALIGN = 2,          /* pointer or stride alignment violated        */
+  H3B_ERR_DTYPE = 3,          /* unsupported element type code               */
+  H3B_ERR_LAUNCH = 4,         /* cudaLaunch / driver entry point failure     */
+  H3B_ERR_TMAP = 5,           /* cuTensorMapEncodeTiled rejected a map       */
+  H3B_ERR_DEVICE_TIMEOUT = 6, /* a bounded device wait ran out               */
+  H3B_ERR_DEVICE = 7,         /* device reported a failure (see status)      */
+  H3B_ERR_ARG = 8             /* null pointer or bad scalar argument         */
+};
+
+/* Element type codes for activation inputs. */
+enum { H3B_BF16 = 0, H3B_F16 = 1 };
+
+/* GEMM epilogue modes (applied in fp32 before the single bf16 rounding). */
+enum {
+  H3B_EPI_STORE = 0,    /* y = acc*scales (+ bias)                            */
+  H3B_EPI_GELU = 1,     /* y = gelu_erf(acc*scales (+ bias))                  */
+  H3B_EPI_GATE_RES = 2  /* y[m,n] = resid[m,n] + (acc*scales (+bias)) * gate[n] */
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+H3B_API int h3b_version(void);
+
+/*
+ * Reads (and with clear != 0 resets) the device status words of every kernel
+ * family: out[0] = first error code, out[1] = site, out[2] = info, out[3] =
+ * block.  Synchronises the current device.
+ */
+H3B_API int h3b_device_status(int32_t* out4, int clear);
+
+/* ---------------------------------------------------------------- INT8 W8A8 */
+
+/*
+ * Per-row dynamic INT8 quantisation: amax = max|x[r,:]| clamped to 1e-12,
+ * scale[r] = amax/127, q = round_half_even(x/scale) clamped to [-128,127].
+ * Replaces ops/int8_convrot.py:99-111 (_dynamic_quant_rows, the host fallback
+ * of torch_npu.npu_dynamic_quant).  x: [m, k] rows `ldx` elements apart,
+ * dtype H3B_BF16 or H3B_F16; q: [m, k] int8 dense; scale: [m] fp32.
+ * k % 8 == 0, ldx % 8 == 0, x 16-byte aligned.
+ */
+H3B_API int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int8_t* q,
+                      float* scale, h3b_stream_t stream);
+
+/*
+ * W8A8 GEMM on tcgen05 kind::i8 with int32 accumulation in TMEM:
+ * y[m,n] = epi(acc[m,n] * xs[m] * ws[n] + bias[n]) as bf16, acc = sum_k
+ * q[m,k]*w[n,k].  Replaces ops/int8_convrot.py:75-96 (torch_npu.
+ * npu_quant_matmul with pertoken_scale, output_dtype bf16).
+ * q: [m,k] int8, w: [n,k] int8 (the module's [N,K] weight, no transpose),
+ * xs: [m] fp32, ws: [n] fp32, bias: [n] bf16 or NULL, y: [m,n] bf16 (row
+ * stride ldy).  resid/gate are used by H3B_EPI_GATE_RES only (resid [m,n]
+ * bf16 with row stride ldy, may alias y; gate [n] bf16).
+ * k % 128 == 0, n % 32 == 0, ldy % 8 == 0.
+ */
+H3B_API int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* w, const float* ws, const void* bias,
+                     void* y, int64_t ldy, const void* resid, const void* gate, int epilogue, int64_t m,
+                     int64_t n, int64_t k, h3b_stream_t stream);
+
+/*
+ * Same GEMM, raw int32 accumulators acc[m,n] (row stride n) for bit-exact
+ * checks of the tensor-core path against sum_k q*w.
+ */
+H3B_API int h3b_gemm_i8_acc_i32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t m, int64_t n, int64_t k,
+                        h3b_stream_t stream);
+
+/* ------------------------------------------------------------------- NVFP4 */
+
+/*
+ * amax_out[0] = max over i of |x[i]| for n bf16 values (x 16-byte aligned,
+ * n % 8 == 0).  amax_out is overwritten (not accumulated).  Global-scale pass
+ * of the NVFP4 activation quantiser; no reference counterpart (the reference
+ * never quantises activations to NVFP4, ops/nvfp4.py:154-173 is W4A16).
+ */
+H3B_API int h3b_amax_bf16(const void* x, int64_t n, float* amax_out, h3b_stream_t stream);
+
+/*
+ * NVFP4 quantiser (e2m1 codes, one e4m3 scale per 16 elements along k, fp32
+ * global scale gs = amax/(6*448), gs = 1 when amax == 0):
+ *   s_b = e4m3_rn_satfinite(amax_b / (6*gs)),  code = e2m1_rne_sat(x/(s_b*gs)).
+ * codes: [m, k/2] bytes; hi_first != 0 stores the even element in the high
+ * nibble (the checkpoint order decoded by ops/nvfp4.py:113-121), 0 stores it
+ * in the low nibble (tensor-core order).  sf: block scales in the 128x4
+ * "blocked" layout decoded by ops/nvfp4.py:46-62 (from_blocked), padded to
+ * (ceil(m/128)*128) x (ceil(k/64)*4) bytes; padding bytes are written as 0.
+ * gs_out[0] receives gs.  The reference holds no quantiser: this follows the
+ * published NVFP4 recipe that its decode (ops/nvfp4.py:86-151) inverts.
+ * k % 64 == 0.
+ */
+H3B_API int h3b_quant_nvfp4(const void* x, int64_t m, int64_t k, int64_t ldx, const float* amax, uint8_t* codes,
+                    uint8_t* sf, float* gs_out, int hi_first, h3b_stream_t stream);
+
+/*
+ * Swap the two nibbles of every byte (checkpoint hi-first order <-> tensor-core
+ * lo-first order).  One-time weight repack, the NVFP4 analogue of
+ * QuantLinear.prepare_cube (modules/linear.py:171-181).  src may equal dst.
+ */
+H3B_API int h3b_nvfp4_swap_nibbles(const uint8_t* src, uint8_t* dst, int64_t nbytes, h3b_stream_t stream);
+
+/*
+ * W4A4 NVFP4 GEMM on tcgen05 kind::mxf4nvf4 (block16, ue4m3 scales in TMEM):
+ * y[m,n] = epi(a_gs*w_gs * sum_k A[m,k]*W[n,k] + bias[n]) as bf16, where
+ * A = dequant(a_codes, a_sf), W = dequant(w_codes, w_sf), codes in lo-first
+ * order, scales in the blocked layout above.  Replaces ops/nvfp4.py:154-173
+ * (nvfp4_linear: dequantize_nvfp4 + F.linear) with the activation quantised
+ * as well.  a_gs / w_gs: device fp32 scalars.  Other arguments as
+ * h3b_gemm_i8_bf16.  k % 256 == 0, n % 32 == 0.
+ */
+H3B_API int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs, const uint8_t* w_codes,
+                        const uint8_t* w_sf, const float* w_gs, const void* bias, void* y, int64_t ldy,
+                        const void* resid, const void* gate, int epilogue, int64_t m, int64_t n, int64_t k,
+                        h3b_stream_t stream);
+
+/* --------------------------------------------------------------- attention */
+
+/*
+ * Non-causal flash attention forward, head_dim 128, bf16 in/out, fp32
+ * softmax and accumulation on tcgen05 kind::f16:
+ *   o[s,h,:] = softmax_j(scale * q[s,h,:].k[j,h,:]) v[j,h,:]
+ * Element (s,h,d) of q lives at q + s*q_seq_stride + h*q_head_stride + d
+ * (likewise k, v, o), so both the packed-QKV token-major layout [S,3,H,D]
+ * and BNSD [H,S,D] are accepted without copies.  lse (optional, [heads, s_q]
+ * fp32, natural log) receives the row log-sum-exp.  Replaces
+ * ops/fa_h3.py:224-304 (h3_attention_bnsd) and ops/attention.py:100-131
+ * (fusion_attention_bnsd), whose host path is F.scaled_dot_product_attention.
+ * Strides % 8 == 0, pointers 16-byte aligned.
+ */
+H3B_API int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t heads,
+                      int64_t s_q, int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
+                      int64_t kv_seq_stride, int64_t kv_head_stride, int64_t o_seq_stride,
+                      int64_t o_head_stride, float scale, h3b_stream_t stream);
+
+/*
+ * In-place q/k RMSNorm (fp32 math, weight [128] bf16, eps) followed by
+ * split-half RoPE over all 128 dims in bf16 arithmetic with a bf16 rotation
+ * table, exactly as ops/rope.py:7-55 (rope_rotation_table + rms_rope_apply)
+ * computes it.  The table is built on the fly: angle[s,j] = pos[s,axis(j)] *
+ * inv_freq[j] for j < 64 (fp32), where j < n_t uses axis 0 (t), j < n_t+n_h
+ * axis 1 (h), else axis 2 (w) — the layout of model/dit.py:746-752
+ * (rope_freqs).  pos: [s_total,3] fp32 grid positions, row s of q/k uses
+ * pos[pos_offset + s].  q/k element (s,h,d) at base + s*seq_stride +
+ * h*head_stride + d.  k may be NULL.
+ */
+H3B_API int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, int64_t seq_stride, int64_t head_stride,
+                        const void* q_weight, const void* k_weight, float eps, const float* pos,
+                        int64_t pos_offset, const float* inv_freq, int n_t, int n_h, h3b_stream_t stream);
+
+/* ------------------------------------------------------- block elementwise */
+
+/*
+ * h[r,:] = rmsnorm(x[r,:]) * w * (1 + scale_row) + shift_row, the fused
+ * norm1/norm2 + _mod_scale_shift of model/dit.py:332-335,433-438 and
+ * modules/linear.py:15-32.  Rows [seg_a, seg_b) use modulation row `row`
+ * only; the caller issues one launch per (a, b, row) segment.  x, h: [m,
+ * hidden] bf16 with row stride ld; w, shift, scale: [hidden] bf16 (shift and
+ * scale point at the selected row).  Writes bf16 h, and when amax_out is not
+ * NULL also atomically max-reduces |h| into amax_out[0] (which the caller
+ * zeroes first) for the NVFP4 global scale.
+ */
+H3B_API int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidden, int64_t ld, const void* w,
+                         const void* shift, const void* scale, float eps, float* amax_out,
+                         h3b_stream_t stream);
+
+/*
+ * x[r,:] += y[r,:] * gate  (bf16, in place), the _mod_gate of
+ * model/dit.py:338-341 for one segment.  gate: [hidden] bf16.
+ */
+H3B_API int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidden, int64_t ld, const void* gate,
+                      h3b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */

@@ -1,0 +1,249 @@
+// Row-wise elementwise kernels of the DiT block (HBM-bound).
+//
+//  * qk_rmsnorm_rope: q/k RMSNorm + split-half RoPE in one pass over each
+//    (token, head) row, the rotation table built on the fly from the token's
+//    (t, h, w) grid position (ops/rope.py:7-55, model/dit.py:746-752).  The
+//    rotation uses the reference's bf16 arithmetic: bf16 cos/sin table, each
+//    product and the sum rounded to bf16.
+//  * rmsnorm_modulate: RMSNorm(hidden) then h*(1+scale)+shift with the
+//    reference's bf16 rounding after each step (model/dit.py:332-335,
+//    modules/linear.py:29-32), optional |h| max for the NVFP4 global scale.
+//  * gate_residual: x += y*gate (model/dit.py:338-341).
+#include "h3b_common.cuh"
+#include "h3b_host.hpp"
+
+namespace {
+
+H3B_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// One warp per (token, head) row of 128 bf16: lane l owns d = 4l..4l+3.
+__global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
+    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t s_len, int heads, int64_t seq_stride,
+    int64_t head_stride, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
+    const float* __restrict__ pos, int64_t pos_offset, const float* __restrict__ inv_freq, int n_t, int n_h) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t rows = s_len * heads * (k != nullptr ? 2 : 1);
+  if (row >= rows) return;
+  const int64_t per = s_len * heads;
+  const bool is_k = row >= per;
+  const int64_t r = is_k ? row - per : row;
+  const int64_t s = r / heads;
+  const int h = static_cast<int>(r - s * heads);
+  __nv_bfloat16* base = (is_k ? k : q) + s * seq_stride + static_cast<int64_t>(h) * head_stride;
+  const __nv_bfloat16* w = is_k ? kw : qw;
+
+  // element j (lane < 16: j = 4*lane.. in the first half; lane >= 16: second half)
+  const uint2 raw = *reinterpret_cast<const uint2*>(base + lane * 4);
+  float x[4] = {bf16lo_to_f32(raw.x), bf16hi_to_f32(raw.x), bf16lo_to_f32(raw.y), bf16hi_to_f32(raw.y)};
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  ss = warp_sum(ss);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, 128.0f) + eps));
+  const uint2 wraw = *reinterpret_cast<const uint2*>(w + lane * 4);
+  const float wv[4] = {bf16lo_to_f32(wraw.x), bf16hi_to_f32(wraw.x), bf16lo_to_f32(wraw.y), bf16hi_to_f32(wraw.y)};
+  float n[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) n[e] = bf16r(__fmul_rn(__fmul_rn(x[e], rstd), wv[e]));
+  // partner element j +- 64 lives in lane +- 16, same slot
+  float p[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) p[e] = __shfl_xor_sync(0xffffffffu, n[e], 16);
+  const float* ps = pos + (pos_offset + s) * 3;
+  const bool first = lane < 16;
+  float out[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int jj = (lane & 15) * 4 + e;  // frequency index 0..63
+    const int axis = jj < n_t ? 0 : (jj < n_t + n_h ? 1 : 2);
+    const float ang = __fmul_rn(ps[axis], inv_freq[jj]);
+    const float c = bf16r(cosf(ang));
+    const float sn = bf16r(sinf(ang));
+    // first half:  c*x[j] + (-s)*x[j+64];  second half: s*x[j] + c*x[j+64]
+    if (first) {
+      out[e] = bf16r(bf16r(c * n[e]) + bf16r(-sn * p[e]));
+    } else {
+      out[e] = bf16r(bf16r(sn * p[e]) + bf16r(c * n[e]));
+    }
+  }
+  uint2 o;
+  o.x = pack_bf16x2(out[0], out[1]);
+  o.y = pack_bf16x2(out[2], out[3]);
+  *reinterpret_cast<uint2*>(base + lane * 4) = o;
+}
+
+// CTAs of 256 threads stride over rows; a row is held in registers (<= MAXV
+// x 8 bf16 per thread).  The optional |h| max is reduced per CTA and published
+// with one atomic.
+template <int MAXV>
+__global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
+    const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ h, int64_t m, int64_t hidden, int64_t ld,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ shift,
+    const __nv_bfloat16* __restrict__ scale, float eps, float* __restrict__ amax_out) {
+  __shared__ float red[33];
+  const int nvec = static_cast<int>(hidden >> 3);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float amax = 0.0f;
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+  const __nv_bfloat16* xr = x + row * ld;
+  uint4 v[MAXV];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = threadIdx.x + i * 256;
+    if (vi < nvec) {
+      v[i] = *reinterpret_cast<const uint4*>(xr + vi * 8);
+      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = bf16lo_to_f32(u[e]), b = bf16hi_to_f32(u[e]);
+        ss += a * a + b * b;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < 8 ? red[lane] : 0.0f;
+    t = warp_sum(t);
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(red[32], static_cast<float>(hidden)) + eps));
+  __syncthreads();  // red[] is reused by the next row
+  __nv_bfloat16* hr = h + row * ld;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = threadIdx.x + i * 256;
+    if (vi < nvec) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
+      const uint4 sh = *reinterpret_cast<const uint4*>(shift + vi * 8);
+      const uint4 sc = *reinterpret_cast<const uint4*>(scale + vi * 8);
+      const uint32_t xu[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t shu[4] = {sh.x, sh.y, sh.z, sh.w};
+      const uint32_t scu[4] = {sc.x, sc.y, sc.z, sc.w};
+      uint32_t outw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float o2[2];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const float xv = half ? bf16hi_to_f32(xu[e]) : bf16lo_to_f32(xu[e]);
+          const float wvv = half ? bf16hi_to_f32(wu[e]) : bf16lo_to_f32(wu[e]);
+          const float shv = half ? bf16hi_to_f32(shu[e]) : bf16lo_to_f32(shu[e]);
+          const float scv = half ? bf16hi_to_f32(scu[e]) : bf16lo_to_f32(scu[e]);
+          const float nrm = bf16r(__fmul_rn(__fmul_rn(xv, rstd), wvv));
+          const float mod = bf16r(bf16r(nrm * bf16r(1.0f + scv)) + shv);
+          amax = fmaxf(amax, fabsf(mod));
+          o2[half] = mod;
+        }
+        outw[e] = pack_bf16x2(o2[0], o2[1]);
+      }
+      *reinterpret_cast<uint4*>(hr + vi * 8) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+    }
+  }
+  }
+  if (amax_out != nullptr) {
+    amax = warp_max(amax);
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    if (warp == 0) {
+      float t = lane < 8 ? red[lane] : 0.0f;
+      t = warp_max(t);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), __float_as_uint(t));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) gate_residual_kernel(__nv_bfloat16* __restrict__ x,
+                                                            const __nv_bfloat16* __restrict__ y, int64_t m,
+                                                            int64_t hidden, int64_t ld,
+                                                            const __nv_bfloat16* __restrict__ gate) {
+  const int64_t nvec_row = hidden >> 3;
+  const int64_t total = m * nvec_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * 256) {
+    const int64_t r = i / nvec_row, c = (i - r * nvec_row) * 8;
+    uint4* xp = reinterpret_cast<uint4*>(x + r * ld + c);
+    const uint4 xv = *xp;
+    const uint4 yv = *reinterpret_cast<const uint4*>(y + r * ld + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gate + c);
+    const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, yu[4] = {yv.x, yv.y, yv.z, yv.w},
+                   gu[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[e] = pack_bf16x2(__fadd_rn(bf16lo_to_f32(xu[e]), __fmul_rn(bf16lo_to_f32(yu[e]), bf16lo_to_f32(gu[e]))),
+                         __fadd_rn(bf16hi_to_f32(xu[e]), __fmul_rn(bf16hi_to_f32(yu[e]), bf16hi_to_f32(gu[e]))));
+    }
+    *xp = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace
+
+extern "C" int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, int64_t seq_stride,
+                                   int64_t head_stride, const void* q_weight, const void* k_weight, float eps,
+                                   const float* pos, int64_t pos_offset, const float* inv_freq, int n_t, int n_h,
+                                   h3b_stream_t stream) {
+  if (q == nullptr || q_weight == nullptr || pos == nullptr || inv_freq == nullptr) return H3B_ERR_ARG;
+  if (k != nullptr && k_weight == nullptr) return H3B_ERR_ARG;
+  if (s < 0 || heads <= 0 || n_t < 0 || n_h < 0 || n_t + n_h > 64 || pos_offset < 0) return H3B_ERR_SHAPE;
+  if ((seq_stride % 4) != 0 || (head_stride % 4) != 0) return H3B_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(q) & 7u) || (k != nullptr && (reinterpret_cast<uintptr_t>(k) & 7u)))
+    return H3B_ERR_ALIGN;
+  if (s == 0) return H3B_OK;
+  const int64_t rows = s * heads * (k != nullptr ? 2 : 1);
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
+  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), s, static_cast<int>(heads), seq_stride,
+      head_stride, static_cast<const __nv_bfloat16*>(q_weight), static_cast<const __nv_bfloat16*>(k_weight), eps,
+      pos, pos_offset, inv_freq, n_t, n_h);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidden, int64_t ld, const void* w,
+                                    const void* shift, const void* scale, float eps, float* amax_out,
+                                    h3b_stream_t stream) {
+  if (x == nullptr || h == nullptr || w == nullptr || shift == nullptr || scale == nullptr) return H3B_ERR_ARG;
+  if (m < 0 || hidden <= 0 || (hidden % 8) != 0 || ld < hidden || (ld % 8) != 0 || m > 0x7fffffff)
+    return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || !h3b::aligned16(h) || !h3b::aligned16(w) || !h3b::aligned16(shift) ||
+      !h3b::aligned16(scale))
+    return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* hb = static_cast<__nv_bfloat16*>(h);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  const auto* sh = static_cast<const __nv_bfloat16*>(shift);
+  const auto* sc = static_cast<const __nv_bfloat16*>(scale);
+  const int64_t nvec = hidden / 8;
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * 8;
+  if (blocks > m) blocks = m;
+  const unsigned g = static_cast<unsigned>(blocks);
+  if (nvec <= 256 * 2)
+    rmsnorm_modulate_kernel<2><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, eps, amax_out);
+  else if (nvec <= 256 * 8)
+    rmsnorm_modulate_kernel<8><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, eps, amax_out);
+  else
+    return H3B_ERR_SHAPE;
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidden, int64_t ld, const void* gate,
+                                 h3b_stream_t stream) {
+  if (x == nullptr || y == nullptr || gate == nullptr) return H3B_ERR_ARG;
+  if (m < 0 || hidden <= 0 || (hidden % 8) != 0 || ld < hidden || (ld % 8) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || !h3b::aligned16(y) || !h3b::aligned16(gate)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  int64_t blocks = (m * (hidden / 8) + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(h3b::num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  gate_residual_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), m, hidden, ld,
+      static_cast<const __nv_bfloat16*>(gate));
+  return h3b::launch_status();
+}

@@ -1,0 +1,438 @@
+// Quantised GEMMs of the DiT-block linears on 5th-generation tensor cores.
+//
+//   INT8  (W8A8):  kind::i8, int32 accumulators in TMEM, epilogue
+//                  y = acc * xs[m] * ws[n] (+ bias[n])  — the semantics of
+//                  torch_npu.npu_quant_matmul at ops/int8_convrot.py:86-93.
+//   NVFP4 (W4A4):  kind::mxf4nvf4.block_scale.block16, e2m1 operands with one
+//                  ue4m3 scale per 16 elements copied smem -> TMEM with
+//                  tcgen05.cp, epilogue y = acc * a_gs * w_gs (+ bias[n]).
+//
+// Structure (one CTA per SM, persistent over 128x256 output tiles):
+//   warp 0      TMA producer: A tile 128x128B, B tile 256x128B (+ scale
+//               factors by plain bulk copies) into a STAGES-deep smem ring.
+//   warp 1      TMEM allocator and single-thread MMA issuer; tcgen05.commit
+//               releases smem slots and publishes finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld 32x32b (one output row per thread),
+//               fp32 dequant/bias/activation/gate-residual, bf16 stores.
+// Operands are K-major with the 128-byte swizzle on both the TMA and the UMMA
+// side.  Loads never use cluster multicast.  Every wait is bounded.
+#include "h3b_common.cuh"
+#include "h3b_host.hpp"
+
+H3B_DECLARE_STATUS();
+H3B_REGISTER_STATUS_READER(gemm);
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
+constexpr int B_BYTES = BN * 128;
+constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
+constexpr int SFB_BYTES = 4096;    // 256 rows x 16 scales
+constexpr int EPI_THREADS = 128;
+constexpr int THREADS = 64 + EPI_THREADS;
+
+enum Kind { KIND_I8 = 0, KIND_NVF4 = 1 };
+enum OutMode { OUT_BF16 = 0, OUT_I32 = 1 };
+
+struct GemmArgs {
+  const float* xs;     // i8: per-row activation scale [m]
+  const float* ws;     // i8: per-column weight scale [n]
+  const float* a_gs;   // nvf4: activation global scale (device scalar)
+  const float* w_gs;   // nvf4: weight global scale (device scalar)
+  const uint8_t* a_sf; // nvf4: blocked scales of A
+  const uint8_t* w_sf; // nvf4: blocked scales of B
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* resid;
+  const __nv_bfloat16* gate;
+  void* y;
+  int64_t ldy;
+  int m, n, k;         // k in elements
+  int epilogue;
+  int out_mode;
+};
+
+template <int KIND>
+struct Cfg {
+  static constexpr int NACC = KIND == KIND_I8 ? 2 : 1;          // accumulator buffers
+  static constexpr int SF_COL0 = NACC * BN;                      // TMEM column of the SF ring
+  static constexpr int SF_COLS_PER_STAGE = 48;                   // 16 (A) + 32 (B)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + (KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0);
+  static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
+  static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM, BN) : idesc_nvf4(BM, BN);
+};
+
+struct __align__(8) Barriers {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int consumed;  // k-slabs whose full barrier the MMA thread has observed
+};
+
+template <int KIND>
+constexpr size_t smem_bytes() {
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * Cfg<KIND>::STAGE_BYTES + sizeof(Barriers);
+}
+
+H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+// Lane 0 waits, the verdict is broadcast so the whole warp stays converged.
+H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                const GemmArgs args) {
+  using C = Cfg<KIND>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sSFA = sB + STAGES * B_BYTES;                 // used by KIND_NVF4 only
+  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * C::STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (args.m + BM - 1) / BM;
+  const int n_tiles = args.n / BN + ((args.n % BN) ? 1 : 0);
+  const int num_tiles = m_tiles * n_tiles;
+  const int nk = args.k / C::K_PER_STAGE;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], EPI_THREADS);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    bars->consumed = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const int round = it / STAGES;
+          if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1, &g_status, 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * 128, m0, &bars->full[s]);
+          tma_load_2d(sB + s * B_BYTES, &tmap_b, kb * 128, n0, &bars->full[s]);
+          if constexpr (KIND == KIND_NVF4) {
+            const int64_t ncb = args.k / 64;  // 64-element scale groups per row
+            const uint8_t* sfa = args.a_sf + ((static_cast<int64_t>(m0 / 128) * ncb) + kb * 4) * 512;
+            const uint8_t* sfb0 = args.w_sf + ((static_cast<int64_t>(n0 / 128) * ncb) + kb * 4) * 512;
+            // A 128-column tail tile has no second scale block: reload the
+            // first one (in bounds); those output columns are never stored.
+            const int nb1 = (n0 + 128 < args.n) ? n0 / 128 + 1 : n0 / 128;
+            const uint8_t* sfb1 = args.w_sf + ((static_cast<int64_t>(nb1) * ncb) + kb * 4) * 512;
+            bulk_load(sSFA + s * SFA_BYTES, sfa, SFA_BYTES, &bars->full[s]);
+            bulk_load(sSFB + s * SFB_BYTES, sfb0, SFB_BYTES / 2, &bars->full[s]);
+            bulk_load(sSFB + s * SFB_BYTES + SFB_BYTES / 2, sfb1, SFB_BYTES / 2, &bars->full[s]);
+          }
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Drain: wait (bounded) for every slab issued but not yet consumed, so
+        // no bulk copy is still writing this CTA's shared memory at exit.
+        const int consumed = *reinterpret_cast<volatile int*>(&bars->consumed);
+        for (int j = consumed; j < it; ++j) {
+          mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local % C::NACC;
+        const int use = local / C::NACC;
+        if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&bars->full[s], (it / STAGES) & 1, &g_status, 3, abort_flag)) {
+            ok = false;
+            break;
+          }
+          *reinterpret_cast<volatile int*>(&bars->consumed) = it + 1;
+          tc_fence_after();
+          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(sA + s * A_BYTES));
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(sB + s * B_BYTES));
+          if constexpr (KIND == KIND_I8) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
+            }
+          } else {
+            const uint32_t sf_col = tmem_base + C::SF_COL0 + s * C::SF_COLS_PER_STAGE;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tc_cp_32x128b_x4(sf_col + j * 4, sdesc_plain_rows16(smem_u32(sSFA + s * SFA_BYTES + j * 512)));
+              tc_cp_32x128b_x4(sf_col + 16 + j * 8,
+                               sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + j * 512)));
+              tc_cp_32x128b_x4(sf_col + 16 + j * 8 + 4,
+                               sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + SFB_BYTES / 2 + j * 512)));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4, sf_col + 16 + j * 8,
+                          (kb | j) != 0);
+            }
+          }
+          tc_commit(&bars->empty[s]);  // slot reusable once these MMAs have read it
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_full[buf]);  // accumulator complete
+      }
+      // Drain all MMAs this thread issued before TMEM is released.
+      tc_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local % C::NACC;
+      const int use = local / C::NACC;
+      if (!warp_wait(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * BM;
+      const int n0 = (tile % n_tiles) * BN;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < args.m;
+      float row_scale = 1.0f;
+      if constexpr (KIND == KIND_I8) {
+        if (args.out_mode == OUT_BF16 && row_ok) row_scale = args.xs[row];
+      } else {
+        row_scale = (*args.a_gs) * (*args.w_gs);
+      }
+      const uint32_t t_row = tmem_base + buf * BN + (static_cast<uint32_t>(quad * 32) << 16);
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tc_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&bars->acc_empty[buf]);
+        }
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= args.n) continue;
+        if (args.out_mode == OUT_I32) {
+          int32_t* out = static_cast<int32_t*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            *reinterpret_cast<uint4*>(out + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          }
+          continue;
+        }
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          // Explicit _rn ops: no FMA contraction, so the INT8 epilogue is
+          // bit-reproducible as (acc*xs)*ws + bias in fp32.
+          float a;
+          if constexpr (KIND == KIND_I8) {
+            a = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), row_scale),
+                          __ldg(args.ws + col0 + j));
+          } else {
+            a = __fmul_rn(__uint_as_float(r[j]), row_scale);
+          }
+          if (args.bias != nullptr) a = __fadd_rn(a, __bfloat162float(args.bias[col0 + j]));
+          v[j] = a;
+        }
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
+        if (args.epilogue == H3B_EPI_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        } else if (args.epilogue == H3B_EPI_GATE_RES) {
+          const __nv_bfloat16* res = args.resid + static_cast<int64_t>(row) * args.ldy + col0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(res + j);
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              v[j + 2 * e] = __fadd_rn(bf16lo_to_f32(rw[e]),
+                                       __fmul_rn(v[j + 2 * e], __bfloat162float(args.gate[col0 + j + 2 * e])));
+              v[j + 2 * e + 1] = __fadd_rn(
+                  bf16hi_to_f32(rw[e]), __fmul_rn(v[j + 2 * e + 1], __bfloat162float(args.gate[col0 + j + 2 * e + 1])));
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          *reinterpret_cast<uint4*>(out + j) =
+              make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int KIND>
+int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
+                cudaStream_t st) {
+  CUtensorMap ta, tb;
+  int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != H3B_OK) return rc;
+  rc = h3b::encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, b_row_bytes, args.n, b_row_bytes, 128, BN,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != H3B_OK) return rc;
+  const size_t smem = smem_bytes<KIND>();
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[KIND]) {
+    if (cudaFuncSetAttribute(gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return H3B_ERR_LAUNCH;
+    attr_set[KIND] = true;
+  }
+  const int m_tiles = static_cast<int>((args.m + BM - 1) / BM);
+  const int n_tiles = static_cast<int>((args.n + BN - 1) / BN);
+  const int tiles = m_tiles * n_tiles;
+  const int grid = tiles < h3b::num_sms() ? tiles : h3b::num_sms();
+  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, args);
+  return h3b::launch_status();
+}
+
+int check_common(int64_t m, int64_t n, int64_t k, int64_t kmul) {
+  if (m <= 0 || n <= 0 || k <= 0) return H3B_ERR_SHAPE;
+  if ((k % kmul) != 0 || (n % 32) != 0) return H3B_ERR_SHAPE;
+  if (m > (1ll << 30) || n > (1ll << 30) || k > (1ll << 30)) return H3B_ERR_SHAPE;
+  return H3B_OK;
+}
+
+}  // namespace
+
+extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* w, const float* ws,
+                                const void* bias, void* y, int64_t ldy, const void* resid, const void* gate,
+                                int epilogue, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+  if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr || y == nullptr) return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 128);
+  if (rc != H3B_OK) return rc;
+  if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr)) return H3B_ERR_ARG;
+  if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(y)) return H3B_ERR_ALIGN;
+  if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  a.xs = xs;
+  a.ws = ws;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.resid = static_cast<const __nv_bfloat16*>(resid);
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.y = y;
+  a.ldy = ldy;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.epilogue = epilogue;
+  a.out_mode = OUT_BF16;
+  return launch_gemm<KIND_I8>(q, w, k, k, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_gemm_i8_acc_i32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t m, int64_t n,
+                                   int64_t k, h3b_stream_t stream) {
+  if (q == nullptr || w == nullptr || acc == nullptr) return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 128);
+  if (rc != H3B_OK) return rc;
+  if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(acc)) return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  a.y = acc;
+  a.ldy = n;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.epilogue = H3B_EPI_STORE;
+  a.out_mode = OUT_I32;
+  return launch_gemm<KIND_I8>(q, w, k, k, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                   const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs,
+                                   const void* bias, void* y, int64_t ldy, const void* resid, const void* gate,
+                                   int epilogue, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+  if (a_codes == nullptr || a_sf == nullptr || a_gs == nullptr || w_codes == nullptr || w_sf == nullptr ||
+      w_gs == nullptr || y == nullptr)
+    return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 256);
+  if (rc != H3B_OK) return rc;
+  if ((n % 128) != 0) return H3B_ERR_SHAPE;  // whole 128-row scale blocks for B
+  if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr)) return H3B_ERR_ARG;
+  if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(y) || !h3b::aligned16(a_sf) ||
+      !h3b::aligned16(w_sf))
+    return H3B_ERR_ALIGN;
+  if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  a.a_gs = a_gs;
+  a.w_gs = w_gs;
+  a.a_sf = a_sf;
+  a.w_sf = w_sf;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.resid = static_cast<const __nv_bfloat16*>(resid);
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.y = y;
+  a.ldy = ldy;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.epilogue = epilogue;
+  a.out_mode = OUT_BF16;
+  return launch_gemm<KIND_NVF4>(a_codes, w_codes, k / 2, k / 2, a, reinterpret_cast<cudaStream_t>(stream));
+}

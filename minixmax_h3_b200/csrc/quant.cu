@@ -1,0 +1,302 @@
+// Activation quantisers of the DiT-block hot path (HBM-bound kernels).
+//
+//  * quant_i8_rows: per-row dynamic INT8 (the semantics of the reference's
+//    _dynamic_quant_rows, ops/int8_convrot.py:99-111): one CTA per row, the row
+//    held in registers as 16-byte vectors, warp-shuffle absmax, IEEE division
+//    and round-half-even so the codes are bit-identical to torch on the CPU.
+//  * amax_bf16: grid-stride |x| max with a single atomicMax per CTA.
+//  * quant_nvfp4: 64 elements (four 16-element blocks) per thread; writes
+//    packed e2m1 codes and the 4 scale bytes of those blocks as one 32-bit word
+//    of the 128x4 blocked scale layout (ops/nvfp4.py:46-62).
+#include <cuda_fp8.h>
+
+#include "h3b_common.cuh"
+#include "h3b_host.hpp"
+
+H3B_DECLARE_STATUS();
+H3B_REGISTER_STATUS_READER(quant);
+
+namespace {
+
+template <typename T>
+H3B_DEV float to_f32(T v);
+template <>
+H3B_DEV float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+H3B_DEV float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+
+template <typename T>
+H3B_DEV void unpack8(const uint4& v, float (&f)[8]) {
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f32<T>(e[i]);
+}
+
+H3B_DEV uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Block-wide max of non-negative floats (THREADS multiple of 32, <= 1024).
+template <int THREADS>
+H3B_DEV float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < THREADS / 32 ? red[lane] : 0.0f;
+    w = warp_max(w);
+    if (lane == 0) red[32] = w;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+template <typename T, int THREADS, int MAXV>
+__global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restrict__ x, int64_t k, int64_t ldx,
+                                                                int8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ float red[33];
+  const int64_t row = blockIdx.x;
+  const int nvec = static_cast<int>(k >> 3);
+  const T* xr = x + row * ldx;
+  uint4 v[MAXV];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = threadIdx.x + i * THREADS;
+    if (vi < nvec) {
+      v[i] = ld_nc_v4(xr + static_cast<int64_t>(vi) * 8);
+      float f[8];
+      unpack8<T>(v[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    }
+  }
+  amax = block_max<THREADS>(amax, red);
+  amax = fmaxf(amax, 1e-12f);
+  const float s = __fdiv_rn(amax, 127.0f);
+  int8_t* qr = q + row * k;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = threadIdx.x + i * THREADS;
+    if (vi < nvec) {
+      float f[8];
+      unpack8<T>(v[i], f);
+      uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float r = rintf(__fdiv_rn(f[j], s));
+        r = fminf(fmaxf(r, -128.0f), 127.0f);
+        const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
+        packed[j >> 2] |= b << ((j & 3) * 8);
+      }
+      *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * 8) = make_uint2(packed[0], packed[1]);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+__global__ void __launch_bounds__(256) amax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t nvec,
+                                                        float* __restrict__ out) {
+  __shared__ float red[33];
+  float amax = 0.0f;
+  for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += static_cast<int64_t>(gridDim.x) * 256) {
+    const uint4 v = ld_nc_v4(x + i * 8);
+    float f[8];
+    unpack8<__nv_bfloat16>(v, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+  }
+  amax = block_max<256>(amax, red);
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(amax));
+}
+
+// Exact decode of an e4m3fn byte (finite, non-negative) to fp32.
+H3B_DEV float e4m3_to_f32(uint32_t b) {
+  const uint32_t e = (b >> 3) & 15u, mnt = b & 7u;
+  if (e == 0) return static_cast<float>(mnt) * 0.001953125f;  // mnt * 2^-9
+  return __uint_as_float(((e + 120u) << 23) | (mnt << 20));  // (1 + mnt/8) * 2^(e-7)
+}
+
+// e2m1 magnitude code of |a| with round-half-even and saturation at 6.
+H3B_DEV uint32_t e2m1_mag(float a) {
+  if (a <= 0.25f) return 0u;
+  if (a < 0.75f) return 1u;
+  if (a <= 1.25f) return 2u;
+  if (a < 1.75f) return 3u;
+  if (a <= 2.5f) return 4u;
+  if (a < 3.5f) return 5u;
+  if (a <= 5.0f) return 6u;
+  return 7u;
+}
+
+H3B_DEV float nvfp4_global_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f; }
+
+__global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int64_t m,
+                                                          int64_t k, int64_t ldx, int64_t rows_padded,
+                                                          const float* __restrict__ amax_ptr,
+                                                          uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                                                          float* __restrict__ gs_out, int hi_first) {
+  const int64_t groups = k >> 6;  // 64-element groups per row
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (item >= rows_padded * groups) return;
+  const int64_t row = item / groups;
+  const int64_t g = item - row * groups;
+  const float gs = nvfp4_global_scale(*amax_ptr);
+  if (item == 0) *gs_out = gs;
+  // blocked layout: ((r/128)*ncb + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4, ncb = groups
+  const int64_t sf_off = ((row >> 7) * groups + g) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4;
+  if (row >= m) {
+    *reinterpret_cast<uint32_t*>(sf + sf_off) = 0u;
+    return;
+  }
+  const __nv_bfloat16* xr = x + row * ldx + g * 64;
+  const float six_gs = 6.0f * gs;
+  uint32_t sf_word = 0u;
+  uint32_t out_words[8];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    float f[16];
+    {
+      const uint4 v0 = ld_nc_v4(xr + b * 16);
+      const uint4 v1 = ld_nc_v4(xr + b * 16 + 8);
+      float a0[8], a1[8];
+      unpack8<__nv_bfloat16>(v0, a0);
+      unpack8<__nv_bfloat16>(v1, a1);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        f[j] = a0[j];
+        f[8 + j] = a1[j];
+      }
+    }
+    float amax_b = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax_b = fmaxf(amax_b, fabsf(f[j]));
+    const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(__fdiv_rn(amax_b, six_gs), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t sbits = static_cast<uint32_t>(sb) & 0xFFu;
+    sf_word |= sbits << (8 * b);
+    const float sval = e4m3_to_f32(sbits);
+    const float denom = sval * gs;
+    uint32_t w0 = 0u, w1 = 0u;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      uint32_t code = 0u;
+      if (sval > 0.0f) {
+        const float r = __fdiv_rn(f[j], denom);
+        code = e2m1_mag(fabsf(r)) | (signbit(r) ? 8u : 0u);
+      }
+      const int byte = j >> 1;
+      const bool even = (j & 1) == 0;
+      const uint32_t shift = (even == (hi_first != 0)) ? 4u : 0u;
+      const uint32_t val = code << (shift + 8u * (byte & 3));
+      if (byte < 4)
+        w0 |= val;
+      else
+        w1 |= val;
+    }
+    out_words[2 * b] = w0;
+    out_words[2 * b + 1] = w1;
+  }
+  uint8_t* cr = codes + row * (k >> 1) + g * 32;
+  *reinterpret_cast<uint4*>(cr) = make_uint4(out_words[0], out_words[1], out_words[2], out_words[3]);
+  *reinterpret_cast<uint4*>(cr + 16) = make_uint4(out_words[4], out_words[5], out_words[6], out_words[7]);
+  *reinterpret_cast<uint32_t*>(sf + sf_off) = sf_word;
+}
+
+__global__ void swap_nibbles_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t nvec) {
+  for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += static_cast<int64_t>(gridDim.x) * 256) {
+    uint4 v = src[i];
+    v.x = ((v.x >> 4) & 0x0F0F0F0Fu) | ((v.x << 4) & 0xF0F0F0F0u);
+    v.y = ((v.y >> 4) & 0x0F0F0F0Fu) | ((v.y << 4) & 0xF0F0F0F0u);
+    v.z = ((v.z >> 4) & 0x0F0F0F0Fu) | ((v.z << 4) & 0xF0F0F0F0u);
+    v.w = ((v.w >> 4) & 0x0F0F0F0Fu) | ((v.w << 4) & 0xF0F0F0F0u);
+    dst[i] = v;
+  }
+}
+
+template <typename T>
+int launch_quant_i8(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q, float* scale, cudaStream_t st) {
+  const T* xt = static_cast<const T*>(x);
+  const int64_t nvec = k / 8;
+  if (nvec <= 128 * 4) {
+    quant_i8_rows_kernel<T, 128, 4><<<static_cast<unsigned>(m), 128, 0, st>>>(xt, k, ldx, q, scale);
+  } else if (nvec <= 256 * 6) {
+    quant_i8_rows_kernel<T, 256, 6><<<static_cast<unsigned>(m), 256, 0, st>>>(xt, k, ldx, q, scale);
+  } else if (nvec <= 512 * 12) {
+    quant_i8_rows_kernel<T, 512, 12><<<static_cast<unsigned>(m), 512, 0, st>>>(xt, k, ldx, q, scale);
+  } else {
+    return H3B_ERR_SHAPE;
+  }
+  return h3b::launch_status();
+}
+
+}  // namespace
+
+extern "C" int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int8_t* q,
+                                 float* scale, h3b_stream_t stream) {
+  if (x == nullptr || q == nullptr || scale == nullptr) return H3B_ERR_ARG;
+  if (m < 0 || k <= 0 || (k % 8) != 0 || ldx < k || (ldx % 8) != 0 || m > 0x7fffffff) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) != 0) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (x_dtype == H3B_BF16) return launch_quant_i8<__nv_bfloat16>(x, m, k, ldx, q, scale, st);
+  if (x_dtype == H3B_F16) return launch_quant_i8<__half>(x, m, k, ldx, q, scale, st);
+  return H3B_ERR_DTYPE;
+}
+
+extern "C" int h3b_amax_bf16(const void* x, int64_t n, float* amax_out, h3b_stream_t stream) {
+  if (x == nullptr || amax_out == nullptr) return H3B_ERR_ARG;
+  if (n < 0 || (n % 8) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x)) return H3B_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_out, 0, sizeof(float), st) != cudaSuccess) return H3B_ERR_LAUNCH;
+  if (n == 0) return H3B_OK;
+  const int64_t nvec = n / 8;
+  int64_t blocks = (nvec + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(h3b::num_sms()) * 8;
+  if (blocks > cap) blocks = cap;
+  amax_bf16_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nvec,
+                                                                   amax_out);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_quant_nvfp4(const void* x, int64_t m, int64_t k, int64_t ldx, const float* amax, uint8_t* codes,
+                               uint8_t* sf, float* gs_out, int hi_first, h3b_stream_t stream) {
+  if (x == nullptr || amax == nullptr || codes == nullptr || sf == nullptr || gs_out == nullptr)
+    return H3B_ERR_ARG;
+  if (m <= 0 || k <= 0 || (k % 64) != 0 || ldx < k || (ldx % 8) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || !h3b::aligned16(codes) || (reinterpret_cast<uintptr_t>(sf) & 3u) != 0)
+    return H3B_ERR_ALIGN;
+  const int64_t rows_padded = (m + 127) / 128 * 128;
+  const int64_t items = rows_padded * (k / 64);
+  const int64_t blocks = (items + 255) / 256;
+  if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  quant_nvfp4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), m, k,
+                                                                     ldx, rows_padded, amax, codes, sf, gs_out,
+                                                                     hi_first);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_nvfp4_swap_nibbles(const uint8_t* src, uint8_t* dst, int64_t nbytes, h3b_stream_t stream) {
+  if (src == nullptr || dst == nullptr) return H3B_ERR_ARG;
+  if (nbytes < 0 || (nbytes % 16) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(src) || !h3b::aligned16(dst)) return H3B_ERR_ALIGN;
+  if (nbytes == 0) return H3B_OK;
+  const int64_t nvec = nbytes / 16;
+  int64_t blocks = (nvec + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(h3b::num_sms()) * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  swap_nibbles_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
+                                                                      reinterpret_cast<uint4*>(dst), nvec);
+  return h3b::launch_status();
+}

@@ -1,0 +1,211 @@
+"""Torch-facing wrappers over the C ABI (device memory, streams, shapes).
+
+Each wrapper validates dtypes/devices, allocates its outputs with the caching
+allocator, and launches on the current CUDA stream.  There is no CPU path:
+non-CUDA tensors raise.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from ._lib import call
+
+EPI_STORE, EPI_GELU, EPI_GATE_RES = 0, 1, 2
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("minixmax_h3_b200 ops run on CUDA tensors only (no CPU fallback)")
+
+
+def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
+    """Views x as [m, k] with unit column stride; returns (x2, m, k, ld)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    ld = x2.stride(0) if x2.shape[0] > 1 else x2.shape[1]
+    return x2, x2.shape[0], x2.shape[1], ld
+
+
+# ----------------------------------------------------------------------------- INT8
+
+
+def quant_i8_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row dynamic INT8 quantisation -> (q int8 [m,k], scale fp32 [m])."""
+    _cuda(x)
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("quant_i8_rows expects bf16/fp16 input")
+    x2, m, k, ld = _rows(x)
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    call("h3b_quant_i8_rows", x2.data_ptr(), 0 if x.dtype == torch.bfloat16 else 1, m, k, ld, q.data_ptr(),
+         s.data_ptr(), _stream(x))
+    return q, s
+
+
+def gemm_i8(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor,
+            bias: Optional[torch.Tensor] = None, *, epilogue: int = EPI_STORE,
+            resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = epi(acc * xs[m] * ws[n] + bias) in bf16; w is the [N, K] int8 weight."""
+    _cuda(q, xs, w, ws, bias, resid, gate, out)
+    m, k = q.shape
+    n = w.shape[0]
+    if out is None:
+        out = resid if epilogue == EPI_GATE_RES and resid is not None and out is None else \
+            torch.empty((m, n), dtype=torch.bfloat16, device=q.device)
+    call("h3b_gemm_i8_bf16", q.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), _ptr(bias), out.data_ptr(),
+         out.stride(0), _ptr(resid), _ptr(gate), epilogue, m, n, k, _stream(q))
+    return out
+
+
+def gemm_i8_acc(q: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Raw int32 accumulators sum_k q[m,k]*w[n,k] from the tensor cores."""
+    _cuda(q, w)
+    m, k = q.shape
+    n = w.shape[0]
+    acc = torch.empty((m, n), dtype=torch.int32, device=q.device)
+    call("h3b_gemm_i8_acc_i32", q.data_ptr(), w.data_ptr(), acc.data_ptr(), m, n, k, _stream(q))
+    return acc
+
+
+# ----------------------------------------------------------------------------- NVFP4
+
+
+@dataclass
+class NVFP4Tensor:
+    """Packed NVFP4 operand: codes [rows, k/2] u8, blocked e4m3 scales, fp32 gs."""
+
+    codes: torch.Tensor
+    sf: torch.Tensor
+    gs: torch.Tensor
+    rows: int
+    k: int
+    hi_first: bool
+
+
+def sf_blocked_bytes(rows: int, k: int) -> int:
+    return ((rows + 127) // 128 * 128) * ((k // 16 + 3) // 4 * 4)
+
+
+def amax(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _cuda(x)
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise TypeError("amax expects a contiguous bf16 tensor")
+    if out is None:
+        out = torch.empty((1,), dtype=torch.float32, device=x.device)
+    call("h3b_amax_bf16", x.data_ptr(), x.numel(), out.data_ptr(), _stream(x))
+    return out
+
+
+def quant_nvfp4(x: torch.Tensor, *, hi_first: bool = False,
+                amax_t: Optional[torch.Tensor] = None) -> NVFP4Tensor:
+    """Dynamic NVFP4 quantisation of a bf16 [.., k] tensor (global scale from amax)."""
+    _cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("quant_nvfp4 expects bf16 input")
+    x2, m, k, ld = _rows(x)
+    if amax_t is None:
+        amax_t = amax(x2 if x2.is_contiguous() else x2.contiguous())
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
+    sf = torch.empty((sf_blocked_bytes(m, k),), dtype=torch.uint8, device=x.device)
+    gs = torch.empty((1,), dtype=torch.float32, device=x.device)
+    call("h3b_quant_nvfp4", x2.data_ptr(), m, k, ld, amax_t.data_ptr(), codes.data_ptr(), sf.data_ptr(),
+         gs.data_ptr(), 1 if hi_first else 0, _stream(x))
+    return NVFP4Tensor(codes, sf, gs, m, k, hi_first)
+
+
+def swap_nibbles(u8: torch.Tensor) -> torch.Tensor:
+    _cuda(u8)
+    src = u8.contiguous()
+    dst = torch.empty_like(src)
+    call("h3b_nvfp4_swap_nibbles", src.data_ptr(), dst.data_ptr(), src.numel(), _stream(src))
+    return dst
+
+
+def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = None, *,
+               epilogue: int = EPI_STORE, resid: Optional[torch.Tensor] = None,
+               gate: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = epi(a_gs*w_gs * A @ W^T + bias) in bf16; both operands lo-first."""
+    if a.hi_first or w.hi_first:
+        raise ValueError("gemm_nvfp4 needs tensor-core (lo-first) nibble order; repack with swap_nibbles")
+    _cuda(a.codes, w.codes, bias, resid, gate, out)
+    m, n, k = a.rows, w.rows, a.k
+    if out is None:
+        out = resid if epilogue == EPI_GATE_RES and resid is not None else \
+            torch.empty((m, n), dtype=torch.bfloat16, device=a.codes.device)
+    call("h3b_gemm_nvfp4_bf16", a.codes.data_ptr(), a.sf.data_ptr(), a.gs.data_ptr(), w.codes.data_ptr(),
+         w.sf.data_ptr(), w.gs.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0), _ptr(resid), _ptr(gate),
+         epilogue, m, n, k, _stream(a.codes))
+    return out
+
+
+# ----------------------------------------------------------------------------- attention
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
+              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Non-causal attention over token-major views q [Sq,H,128], k/v [Skv,H,128].
+
+    Any strides with a unit last dimension are accepted (e.g. slices of a packed
+    [S, 3, H, D] QKV buffer).  Returns o [Sq, H, 128] bf16.
+    """
+    _cuda(q, k, v, out, lse)
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[-1] != 128 or t.stride(-1) != 1:
+            raise ValueError("attention expects bf16 [S, H, 128] views with unit last stride")
+    if k.stride() != v.stride():
+        raise ValueError("k and v must share strides")
+    s_q, heads, d = q.shape
+    s_kv = k.shape[0]
+    if out is None:
+        out = torch.empty((s_q, heads, d), dtype=torch.bfloat16, device=q.device)
+    scale = d ** -0.5 if scale is None else float(scale)
+    call("h3b_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse), heads, s_q,
+         s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), out.stride(0), out.stride(1), scale, _stream(q))
+    return out
+
+
+def qk_rmsnorm_rope(q: torch.Tensor, k: Optional[torch.Tensor], q_weight: torch.Tensor,
+                    k_weight: Optional[torch.Tensor], eps: float, pos: torch.Tensor, pos_offset: int,
+                    inv_freq: torch.Tensor, n_t: int, n_h: int) -> None:
+    """In-place RMSNorm + split-half RoPE of q (and k) [S, H, 128] views."""
+    _cuda(q, k, q_weight, k_weight, pos, inv_freq)
+    if k is not None and k.stride() != q.stride():
+        raise ValueError("q and k must share strides")
+    s, heads, d = q.shape
+    call("h3b_qk_rmsnorm_rope", q.data_ptr(), _ptr(k), s, heads, q.stride(0), q.stride(1), q_weight.data_ptr(),
+         _ptr(k_weight), eps, pos.data_ptr(), pos_offset, inv_freq.data_ptr(), n_t, n_h, _stream(q))
+
+
+# ----------------------------------------------------------------------------- block elementwise
+
+
+def rmsnorm_modulate(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float,
+                     out: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _cuda(x, weight, shift, scale, out, amax_out)
+    x2, m, hidden, ld = _rows(x)
+    if out is None:
+        out = torch.empty((m, hidden), dtype=torch.bfloat16, device=x.device)
+    call("h3b_rmsnorm_modulate", x2.data_ptr(), out.data_ptr(), m, hidden, ld, weight.data_ptr(), shift.data_ptr(),
+         scale.data_ptr(), eps, _ptr(amax_out), _stream(x))
+    return out
+
+
+def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    _cuda(x, y, gate)
+    m, hidden = x.shape
+    call("h3b_gate_residual", x.data_ptr(), y.data_ptr(), m, hidden, x.stride(0), gate.data_ptr(), _stream(x))
+    return x

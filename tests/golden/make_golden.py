@@ -1,0 +1,161 @@
+"""Regenerates the golden fixtures in this directory from the REFERENCE's own
+Python (BHUHD/minixmax-h3, imported through oracle/reference.py).
+
+    python tests/golden/make_golden.py
+
+Each fixture stores seeded inputs and the reference's outputs for one hot-path
+function, so the GPU tests can check the CUDA kernels against the reference on
+machines where the reference tree is absent.  Fixtures:
+
+  int8_quant.pt   ops/int8_convrot.py:99-111  _dynamic_quant_rows
+  nvfp4.pt        ops/nvfp4.py:124-151        dequantize_nvfp4 of oracle-quantised codes
+  rope.pt         ops/rope.py:7-55            rope_rotation_table + rms_rope_apply (44/42/42)
+  attention.pt    ops/attention.py:100-131    fusion_attention_bnsd (SDPA host path)
+  dit_block_*.pt  model/dit.py:400-438        DiTBlock.forward with emulated quantised linears
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from oracle import h3_oracle as O  # noqa: E402
+from oracle import reference  # noqa: E402
+
+
+def outlier_activations(g: torch.Generator, m: int, k: int) -> torch.Tensor:
+    """N(0,1) with 0.1% of entries scaled x20 (the benchmark's activation model)."""
+    x = torch.randn(m, k, generator=g)
+    mask = torch.rand(m, k, generator=g) < 0.001
+    return torch.where(mask, x * 20.0, x)
+
+
+def make_int8(R) -> dict:
+    g = torch.Generator().manual_seed(0)
+    x = outlier_activations(g, 46, 3072)
+    x = torch.cat([x, torch.zeros(1, 3072), torch.full((1, 3072), 1e-30)], dim=0).to(torch.bfloat16)
+    q, s = R.int8_convrot._dynamic_quant_rows(x.to(torch.bfloat16))
+    return {"x": x, "q": q, "scale": s}
+
+
+def make_nvfp4(R) -> dict:
+    g = torch.Generator().manual_seed(1)
+    x = outlier_activations(g, 130, 256)
+    x[5] = 0.0
+    x[7, 3] = 300.0
+    x = x.to(torch.bfloat16)
+    qz = O.nvfp4_quantize(x, hi_first=True)
+    sf8 = qz["sf"].view(torch.float8_e4m3fn)
+    deq = R.nvfp4.dequantize_nvfp4(qz["codes"], qz["gs"], sf8, out_dtype=torch.float32)
+    deq_bf16 = R.nvfp4.dequantize_nvfp4(qz["codes"], qz["gs"], sf8, out_dtype=torch.bfloat16)
+    return {"x": x, "codes_hi_first": qz["codes"], "sf": qz["sf"], "gs": qz["gs"], "dequant_f32": deq,
+            "dequant_bf16": deq_bf16}
+
+
+def make_rope(R) -> dict:
+    g = torch.Generator().manual_seed(2)
+    t, h, w = 2, 6, 8
+    pos = O.grid_positions(t, h, w)
+    heads = 3
+    q = torch.randn(1, pos.shape[0], heads, 128, generator=g).to(torch.bfloat16) * 3
+    weight = (1.0 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    inv = O.rope_inv_freq((44, 42, 42))
+    angles = O.rope_angles(pos, inv, 22, 21)
+    table = R.rope.rope_rotation_table(angles, torch.bfloat16)
+    out = R.rope.rms_rope_apply(q, table, weight, 1e-6, 128)
+    return {"q": q, "weight": weight, "pos": pos, "inv_freq": inv, "n_t": 22, "n_h": 21, "eps": 1e-6,
+            "table": table, "out": out}
+
+
+def make_attention(R) -> dict:
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(1, 2, 200, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, 2, 333, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, 2, 333, 128, generator=g).to(torch.bfloat16)
+    out = R.attention.fusion_attention_bnsd(q, k, v)
+    return {"q": q, "k": k, "v": v, "out": out}
+
+
+def block_params(g: torch.Generator, hidden: int, heads: int, ffn_out: int, ffn_in: int, t_dim: int) -> dict:
+    inner = heads * 128
+    p = {
+        "qkv_w": torch.randn(3 * inner, hidden, generator=g) * 0.02,
+        "out_w": torch.randn(hidden, inner, generator=g) * 0.02,
+        "fc1_w": torch.randn(ffn_out, hidden, generator=g) * 0.02,
+        "fc2_w": torch.randn(hidden, ffn_in, generator=g) * 0.02,
+        "adaln_w": torch.randn(6 * hidden * 3, t_dim, generator=g) * 0.02,
+        "adaln_b": torch.randn(6 * hidden * 3, generator=g) * 0.02,
+        "norm1_w": 1.0 + 0.1 * torch.randn(hidden, generator=g),
+        "norm2_w": 1.0 + 0.1 * torch.randn(hidden, generator=g),
+        "q_norm_w": 1.0 + 0.1 * torch.randn(128, generator=g),
+        "k_norm_w": 1.0 + 0.1 * torch.randn(128, generator=g),
+    }
+    return {k: v.to(torch.bfloat16) for k, v in p.items()}
+
+
+def make_block(R, fmt: str, mlp_act: str) -> dict:
+    """Reference DiTBlock with its four projections swapped for the oracle's
+    emulated quantised linear (the only part the reference cannot run on CPU)."""
+    g = torch.Generator().manual_seed(4)
+    hidden, heads, t_dim, eps, qk_eps = 128, 1, 32, 1e-6, 1e-6
+    grid = (1, 8, 8)
+    s_len = grid[0] * grid[1] * grid[2]
+    ffn = 4 * hidden
+    ffn_out = ffn if mlp_act == "gelu" else 2 * ffn
+    p = block_params(g, hidden, heads, ffn_out, ffn, t_dim)
+    x = torch.randn(s_len, hidden, generator=g).to(torch.bfloat16)
+    t = torch.rand(1, generator=g) * 1000.0
+    t_emb = O.timestep_embedding(t, t_dim).to(torch.bfloat16)
+    segments = [(0, s_len // 4, 1), (s_len // 4, s_len, 0)]
+
+    blk = R.dit.DiTBlock(hidden, heads, 128, ffn, t_dim, eps, qk_eps, apply_silu=True, dtype=torch.bfloat16)
+    blk.norm1.weight.data.copy_(p["norm1_w"])
+    blk.norm2.weight.data.copy_(p["norm2_w"])
+    blk.attn.q_norm.weight.data.copy_(p["q_norm_w"])
+    blk.attn.k_norm.weight.data.copy_(p["k_norm_w"])
+    blk.adaln_proj.linear.weight.data.copy_(p["adaln_w"])
+    blk.adaln_proj.linear.bias.data.copy_(p["adaln_b"])
+    lin = {n: O.EmulatedQuantLinear(p[f"{n}_w"], fmt) for n in ("qkv", "out", "fc1", "fc2")}
+    blk.attn.qkv_proj = lin["qkv"]
+    blk.attn.out_proj = lin["out"]
+    blk.mlp.fc1 = lin["fc1"]
+    blk.mlp.fc2 = lin["fc2"]
+    if mlp_act == "gelu":
+        blk.mlp.forward = lambda u: lin["fc2"](F.gelu(lin["fc1"](u)))
+
+    pos = O.grid_positions(*grid)
+    inv = O.rope_inv_freq((44, 42, 42))
+    table = R.rope.rope_rotation_table(O.rope_angles(pos, inv, 22, 21), torch.bfloat16)
+    with torch.no_grad():
+        out = blk(x.clone(), t_emb, segments, table)
+    return {"fmt": fmt, "mlp_act": mlp_act, "hidden": hidden, "heads": heads, "t_dim": t_dim, "eps": eps,
+            "qk_eps": qk_eps, "grid": grid, "segments": segments, "params": p, "x": x, "t_emb": t_emb,
+            "pos": pos, "inv_freq": inv, "n_t": 22, "n_h": 21, "out": out}
+
+
+def main() -> None:
+    R = reference.load()
+    if R is None:
+        raise SystemExit("reference tree not found; set H3B_REFERENCE_ROOT")
+    torch.set_num_threads(1)
+    fixtures = {
+        "int8_quant.pt": make_int8(R),
+        "nvfp4.pt": make_nvfp4(R),
+        "rope.pt": make_rope(R),
+        "attention.pt": make_attention(R),
+        "dit_block_int8_gelu.pt": make_block(R, "int8", "gelu"),
+        "dit_block_nvfp4_gelu.pt": make_block(R, "nvfp4", "gelu"),
+        "dit_block_nvfp4_swiglu.pt": make_block(R, "nvfp4", "swiglu"),
+    }
+    for name, data in fixtures.items():
+        torch.save(data, HERE / name)
+        print(f"wrote {name} ({(HERE / name).stat().st_size / 1024:.0f} KiB)")
+
+
+if __name__ == "__main__":
+    main()

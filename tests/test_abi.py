@@ -1,0 +1,44 @@
+"""CPU: the C-ABI library loads, exports every entry point include/h3b.h
+declares, and rejects bad arguments on the host without touching a GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from minixmax_h3_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "h3b.h"
+
+
+def declared() -> list[str]:
+    return re.findall(r"H3B_API\s+int\s+(h3b_\w+)\s*\(", HEADER.read_text())
+
+
+def test_header_and_binding_agree():
+    names = declared()
+    assert len(names) >= 12
+    assert sorted(names) == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_symbol():
+    lib = _lib.lib()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.h3b_version() >= 100
+
+
+@pytest.mark.parametrize("name,args,code", [
+    ("h3b_quant_i8_rows", (None, 0, 4, 64, 64, None, None, None), 8),
+    ("h3b_gemm_i8_bf16", (1, 1, 1, 1, None, 1, 64, None, None, 0, 4, 48, 128, None), 1),   # n % 32
+    ("h3b_gemm_i8_bf16", (1, 1, 1, 1, None, 1, 64, None, None, 0, 4, 64, 100, None), 1),   # k % 128
+    ("h3b_gemm_nvfp4_bf16", (16, 16, 16, 16, 16, 16, None, 16, 256, None, None, 0, 4, 256, 128, None), 1),
+    ("h3b_quant_nvfp4", (16, 4, 48, 48, 16, 16, 16, 16, 1, None), 1),                       # k % 64
+    ("h3b_attention_fwd", (None,) * 5 + (1, 1, 1, 128, 128, 128, 128, 128, 128, 0.1, None), 8),
+    ("h3b_amax_bf16", (16, 7, 16, None), 1),
+])
+def test_host_side_validation(name, args, code):
+    fn = getattr(_lib.lib(), name)
+    assert fn(*args) == code

@@ -1,0 +1,114 @@
+"""GPU parity: tcgen05 INT8 and NVFP4 GEMMs.
+
+Bars: int32 accumulators bit-exact; INT8 bf16 outputs bit-exact to the
+oracle's fp32 epilogue ((acc*xs)*ws + bias, one bf16 rounding); NVFP4 and
+activation epilogues within helpers.assert_close_bf16 (scaled max-abs <= 2e-2,
+cosine >= 0.9995) of the exact fp64 product of the decoded operands."""
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from helpers import assert_close_bf16
+from oracle import h3_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 256, 128), (300, 288, 384), (1000, 3072, 3072), (64, 512, 12288)]
+
+
+def _i8(seed, *shape):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_i8_acc_bit_exact(cuda, m, n, k):
+    from minixmax_h3_b200 import ops
+
+    q, w = _i8(m, m, k), _i8(n, n, k)
+    acc = ops.gemm_i8_acc(q.to(cuda), w.to(cuda))
+    assert torch.equal(acc.cpu(), O.int8_acc(q, w))
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES[:3])
+def test_i8_linear_bit_exact(cuda, m, n, k):
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w, ws = O.quantize_weight_int8(torch.randn(n, k, generator=g) * 0.02)
+    bias = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    q, xs = ops.quant_i8_rows(x.to(cuda))
+    y = ops.gemm_i8(q, xs, w.to(cuda), ws.to(cuda), bias.to(cuda))
+    q_ref, xs_ref = O.dynamic_quant_rows(x)
+    assert torch.equal(q.cpu(), q_ref)
+    assert torch.equal(y.cpu(), O.w8a8_linear(q_ref, xs_ref, w, ws, bias))
+
+
+def test_i8_cfg2_shapes_sampled(cuda):
+    """BASELINE cfg 2 shapes at full M; 256 random rows checked bit-exact."""
+    from minixmax_h3_b200 import ops
+
+    rows = torch.randperm(32768, generator=torch.Generator().manual_seed(2))[:256]
+    for k, n in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]:
+        q = torch.randint(-128, 128, (32768, k), dtype=torch.int8, device=cuda)
+        w = torch.randint(-128, 128, (n, k), dtype=torch.int8, device=cuda)
+        acc = ops.gemm_i8_acc(q, w)
+        r = rows.to(cuda)
+        assert torch.equal(acc[r].cpu(), O.int8_acc(q[r].cpu(), w.cpu())), (k, n)
+
+
+def test_i8_epilogues(cuda):
+    from minixmax_h3_b200 import ops
+
+    m, n, k = 256, 512, 1024
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w, ws = O.quantize_weight_int8(torch.randn(n, k, generator=g) * 0.02)
+    resid = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    gate = torch.randn(n, generator=g).to(torch.bfloat16)
+    q, xs = ops.quant_i8_rows(x.to(cuda))
+    y_lin = O.w8a8_linear(*O.dynamic_quant_rows(x), w, ws).float()
+    pre = O.int8_acc(*[O.dynamic_quant_rows(x)[0], w]).float() * O.dynamic_quant_rows(x)[1][:, None] * ws[None]
+    gelu = ops.gemm_i8(q, xs, w.to(cuda), ws.to(cuda), epilogue=ops.EPI_GELU)
+    assert_close_bf16(gelu, F.gelu(pre), max_abs=1e-2)
+    r = resid.to(cuda).clone()
+    out = ops.gemm_i8(q, xs, w.to(cuda), ws.to(cuda), epilogue=ops.EPI_GATE_RES, resid=r, gate=gate.to(cuda))
+    assert out.data_ptr() == r.data_ptr()
+    want = (resid.float() + pre * gate.float()).to(torch.bfloat16)
+    assert torch.equal(out.cpu(), want)
+    assert_close_bf16(y_lin, pre)
+
+
+def _nvfp4_operands(cuda, m, n, k, seed):
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g)
+    x = torch.where(torch.rand(m, k, generator=g) < 0.001, 20 * x, x).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    a = ops.quant_nvfp4(x.to(cuda))
+    wq = ops.quant_nvfp4(w.to(cuda))
+    return x, w, a, wq
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (300, 384, 512), (1000, 3072, 3072), (200, 256, 12288)])
+def test_nvfp4_gemm(cuda, m, n, k):
+    from minixmax_h3_b200 import ops
+
+    x, w, a, wq = _nvfp4_operands(cuda, m, n, k, m + n + k)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(1)) * 0.1).to(torch.bfloat16)
+    y = ops.gemm_nvfp4(a, wq, bias.to(cuda))
+    a_or = {"codes": a.codes.cpu(), "sf": a.sf.cpu(), "gs": a.gs.cpu()}
+    w_or = {"codes": wq.codes.cpu(), "sf": wq.sf.cpu(), "gs": wq.gs.cpu()}
+    exact = O.nvfp4_linear_w4a4(a_or, w_or, k, bias, a_hi_first=False, w_hi_first=False)
+    assert_close_bf16(y, exact)
+    # The reference's own arithmetic on the same codes (ops/nvfp4.py:154-173):
+    # decode to bf16, then F.linear.  Rounding every decoded operand to bf16
+    # (relative 2^-9 each) makes that path itself drift from the exact
+    # product as sqrt(K) grows, so this comparison allows 5e-2 (scaled).
+    ad = O.nvfp4_dequantize(a_or["codes"], a_or["gs"], a_or["sf"], k, False).to(torch.bfloat16)
+    wd = O.nvfp4_dequantize(w_or["codes"], w_or["gs"], w_or["sf"], k, False).to(torch.bfloat16)
+    assert_close_bf16(y, F.linear(ad, wd, bias).float(), max_abs=5e-2)

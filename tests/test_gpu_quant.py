@@ -1,0 +1,97 @@
+"""GPU parity: activation quantisers vs the oracle and the reference fixtures.
+
+Bar: INT8 codes/scales and NVFP4 codes/scales are bit-exact."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from helpers import load_golden
+from oracle import h3_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _outliers(seed: int, m: int, k: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g)
+    return torch.where(torch.rand(m, k, generator=g) < 0.001, 20 * x, x).to(torch.bfloat16)
+
+
+def test_int8_golden(cuda):
+    from minixmax_h3_b200 import ops
+
+    g = load_golden("int8_quant.pt")
+    q, s = ops.quant_i8_rows(g["x"].to(cuda))
+    assert torch.equal(q.cpu(), g["q"]) and torch.equal(s.cpu(), g["scale"])
+
+
+@pytest.mark.parametrize("k", [8, 72, 3072, 12288, 40960])
+def test_int8_rows_bit_exact(cuda, k):
+    from minixmax_h3_b200 import ops
+
+    x = _outliers(k, 129, k)
+    q, s = ops.quant_i8_rows(x.to(cuda))
+    q_ref, s_ref = O.dynamic_quant_rows(x)
+    assert torch.equal(q.cpu(), q_ref) and torch.equal(s.cpu(), s_ref)
+
+
+def test_int8_fp16_and_strided(cuda):
+    from minixmax_h3_b200 import ops
+
+    x = _outliers(3, 64, 1024).to(torch.float16)
+    q, s = ops.quant_i8_rows(x.to(cuda))
+    q_ref, s_ref = O.dynamic_quant_rows(x)
+    assert torch.equal(q.cpu(), q_ref) and torch.equal(s.cpu(), s_ref)
+    big = _outliers(4, 64, 2048).to(cuda)
+    q2, s2 = ops.quant_i8_rows(big[:, 512:1536])  # row stride 2048
+    q2_ref, s2_ref = O.dynamic_quant_rows(big[:, 512:1536].cpu())
+    assert torch.equal(q2.cpu(), q2_ref) and torch.equal(s2.cpu(), s2_ref)
+
+
+def test_int8_cfg2_full_size_sampled(cuda):
+    """M=32768 x K=12288 on the GPU; 512 random rows re-derived on the CPU."""
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = torch.randn(32768, 12288, generator=g, device=cuda)
+    x = torch.where(torch.rand(32768, 12288, generator=g, device=cuda) < 0.001, 20 * x, x).to(torch.bfloat16)
+    q, s = ops.quant_i8_rows(x)
+    rows = torch.randperm(32768, generator=torch.Generator().manual_seed(1))[:512]
+    q_ref, s_ref = O.dynamic_quant_rows(x[rows.to(cuda)].cpu())
+    assert torch.equal(q[rows.to(cuda)].cpu(), q_ref) and torch.equal(s[rows.to(cuda)].cpu(), s_ref)
+
+
+def test_nvfp4_golden(cuda):
+    from minixmax_h3_b200 import ops
+
+    g = load_golden("nvfp4.pt")
+    hi = ops.quant_nvfp4(g["x"].to(cuda), hi_first=True)
+    assert torch.equal(hi.codes.cpu(), g["codes_hi_first"])
+    assert torch.equal(hi.sf.cpu(), g["sf"]) and torch.equal(hi.gs.cpu(), g["gs"])
+    lo = ops.quant_nvfp4(g["x"].to(cuda), hi_first=False)
+    assert torch.equal(O.swap_nibbles(lo.codes.cpu()), g["codes_hi_first"])
+    assert torch.equal(ops.swap_nibbles(lo.codes).cpu(), g["codes_hi_first"])
+
+
+@pytest.mark.parametrize("m,k", [(1, 64), (300, 3072), (4096, 3072), (257, 12288)])
+def test_nvfp4_bit_exact(cuda, m, k):
+    from minixmax_h3_b200 import ops
+
+    x = _outliers(m + k, m, k)
+    got = ops.quant_nvfp4(x.to(cuda), hi_first=True)
+    want = O.nvfp4_quantize(x, hi_first=True)
+    assert torch.equal(got.gs.cpu(), want["gs"])
+    assert torch.equal(got.codes.cpu(), want["codes"])
+    assert torch.equal(got.sf.cpu(), want["sf"])
+
+
+def test_amax_and_zero_input(cuda):
+    from minixmax_h3_b200 import ops
+
+    x = _outliers(9, 333, 256)
+    assert ops.amax(x.to(cuda)).item() == x.float().abs().max().item()
+    z = torch.zeros(130, 128, dtype=torch.bfloat16)
+    got = ops.quant_nvfp4(z.to(cuda), hi_first=True)
+    want = O.nvfp4_quantize(z, hi_first=True)
+    assert got.gs.item() == 1.0 and torch.equal(got.codes.cpu(), want["codes"]) and torch.equal(got.sf.cpu(), want["sf"])

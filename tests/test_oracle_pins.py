@@ -1,0 +1,152 @@
+"""CPU: pin the oracle restatement against the reference's own Python and the
+committed golden fixtures (generated from the reference by
+tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from helpers import load_golden
+from oracle import h3_oracle as O
+
+
+def _outliers(seed: int, m: int, k: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g)
+    return torch.where(torch.rand(m, k, generator=g) < 0.001, 20 * x, x).to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------- INT8
+
+def test_int8_quant_matches_reference(ref):
+    for seed, (m, k) in enumerate([(7, 3072), (33, 12288), (5, 8)]):
+        x = _outliers(seed, m, k)
+        q_ref, s_ref = ref.int8_convrot._dynamic_quant_rows(x)
+        q, s = O.dynamic_quant_rows(x)
+        assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+
+
+def test_int8_quant_golden():
+    g = load_golden("int8_quant.pt")
+    q, s = O.dynamic_quant_rows(g["x"])
+    assert torch.equal(q, g["q"]) and torch.equal(s, g["scale"])
+    assert (g["q"][-2] == 0).all() and (g["q"][-1] == 0).all()  # zero row, tiny row (1e-12 clamp)
+
+
+def test_int8_acc_exact():
+    g = torch.Generator().manual_seed(3)
+    q = torch.randint(-128, 128, (17, 256), generator=g, dtype=torch.int8)
+    w = torch.randint(-128, 128, (40, 256), generator=g, dtype=torch.int8)
+    want = (q.to(torch.int64) @ w.to(torch.int64).T).to(torch.int32)
+    assert torch.equal(O.int8_acc(q, w), want)
+    assert torch.equal(O.int8_acc(q, w), torch._int_mm(q.contiguous(), w.T.contiguous()))
+
+
+# ---------------------------------------------------------------- NVFP4
+
+def test_e4m3_decode_matches_reference(ref):
+    bits = torch.arange(256, dtype=torch.int32).to(torch.uint8)
+    want = ref.float8_cast._fp8_e4m3fn_to_f32(bits).numpy()
+    got = O.e4m3_decode(bits.numpy())
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert np.array_equal(got[ok], want[ok])
+
+
+def test_e4m3_encoder_is_round_nearest_even():
+    rng = np.random.default_rng(0)
+    v = np.abs(rng.standard_normal(100_000).astype(np.float32)) * np.float32(60)
+    mids = ((O._E4M3_POS[1:] + O._E4M3_POS[:-1]) / 2).astype(np.float32)
+    v = np.concatenate([v, O._E4M3_POS, mids, np.float32([0, 1e-9, 447, 448, 464, 1e6])]).astype(np.float32)
+    want = torch.from_numpy(np.minimum(v, 448)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(O.e4m3_rn_satfinite(v), want)
+
+
+def test_blocked_layout_matches_reference(ref):
+    g = torch.Generator().manual_seed(5)
+    for rows, ncols in [(130, 16), (256, 192), (7, 4)]:
+        sf = torch.randint(0, 127, (rows, ncols), generator=g, dtype=torch.uint8)
+        flat = torch.from_numpy(O.to_blocked(sf.numpy()))
+        padded = flat.reshape((rows + 127) // 128 * 128, (ncols + 3) // 4 * 4)
+        assert torch.equal(ref.nvfp4.from_blocked(padded, rows, ncols), sf)
+
+
+def test_nvfp4_roundtrip_through_reference_decode(ref):
+    x = _outliers(11, 200, 512)
+    qz = O.nvfp4_quantize(x, hi_first=True)
+    want = ref.nvfp4.dequantize_nvfp4(qz["codes"], qz["gs"], qz["sf"].view(torch.float8_e4m3fn),
+                                      out_dtype=torch.float32)
+    got = O.nvfp4_dequantize(qz["codes"], qz["gs"], qz["sf"], 512, hi_first=True)
+    assert torch.equal(got, want)
+    # quantisation error is bounded by half an e2m1 step of each block's scale
+    assert (got - x.float()).abs().max() <= x.float().abs().max() / 6 * 1.01
+
+
+def test_nvfp4_golden():
+    g = load_golden("nvfp4.pt")
+    qz = O.nvfp4_quantize(g["x"], hi_first=True)
+    assert torch.equal(qz["codes"], g["codes_hi_first"])
+    assert torch.equal(qz["sf"], g["sf"]) and torch.equal(qz["gs"], g["gs"])
+    k = g["x"].shape[1]
+    assert torch.equal(O.nvfp4_dequantize(qz["codes"], qz["gs"], qz["sf"], k), g["dequant_f32"])
+    lo = O.nvfp4_quantize(g["x"], hi_first=False)
+    assert torch.equal(O.swap_nibbles(lo["codes"]), g["codes_hi_first"])
+
+
+# ---------------------------------------------------------------- RoPE / norm
+
+def test_rope_golden():
+    g = load_golden("rope.pt")
+    angles = O.rope_angles(g["pos"], g["inv_freq"], g["n_t"], g["n_h"])
+    table = O.rope_rotation_table(angles, torch.bfloat16)
+    assert torch.equal(table, g["table"])
+    out = O.rms_rope_apply(g["q"], table, g["weight"], g["eps"], 128)
+    assert torch.equal(out, g["out"])
+
+
+def test_rope_matches_reference(ref):
+    g = torch.Generator().manual_seed(8)
+    pos = O.grid_positions(3, 4, 5)
+    x = torch.randn(1, 60, 2, 128, generator=g).to(torch.bfloat16)
+    w = torch.ones(128, dtype=torch.bfloat16)
+    angles = O.rope_angles(pos, O.rope_inv_freq(), 22, 21)
+    t_ref = ref.rope.rope_rotation_table(angles, torch.bfloat16)
+    assert torch.equal(O.rope_rotation_table(angles, torch.bfloat16), t_ref)
+    assert torch.equal(O.rms_rope_apply(x, t_ref, w, 1e-6, 128), ref.rope.rms_rope_apply(x, t_ref, w, 1e-6, 128))
+    assert torch.equal(O.rms_norm(x, w, 1e-5), ref.linear.RMSNorm(128, eps=1e-5)(x))
+
+
+# ---------------------------------------------------------------- attention / block
+
+def test_attention_golden():
+    g = load_golden("attention.pt")
+    o = O.attention_fp32(g["q"][0], g["k"][0], g["v"][0])
+    assert (o - g["out"][0].float()).abs().max() < 2e-2
+
+
+def test_ulysses_layout_matches_reference_permutation():
+    """seq->head: rank r receives every rank's tokens (rank order) for heads
+    [r*H/ws, (r+1)*H/ws) — ops/ulysses.py:28-31 evaluated for all ranks."""
+    ws, s_local, h, d = 4, 3, 8, 2
+    full = torch.arange(ws * s_local * h * d, dtype=torch.float32).reshape(ws * s_local, h, d)
+    shards = full.chunk(ws, dim=0)
+    sends = [x.view(s_local, ws, h // ws, d).permute(1, 0, 2, 3).contiguous() for x in shards]
+    for r in range(ws):
+        recv = torch.stack([sends[src][r] for src in range(ws)])  # all_to_all_single
+        got = recv.reshape(ws * s_local, h // ws, d)
+        assert torch.equal(got, O.seq_to_head_local(full, ws, r))
+
+
+def _block_linear(g, fmt):
+    lin = {n: O.EmulatedQuantLinear(g["params"][f"{n}_w"], fmt) for n in ("qkv", "out", "fc1", "fc2")}
+    return lambda name, x: lin[name](x)
+
+
+def test_dit_block_golden_bit_exact():
+    for name in ("dit_block_int8_gelu.pt", "dit_block_nvfp4_gelu.pt", "dit_block_nvfp4_swiglu.pt"):
+        g = load_golden(name)
+        out = O.dit_block_forward(g["x"].clone(), g["t_emb"], g["segments"], g["params"], heads=g["heads"],
+                                  head_dim=128, eps=g["eps"], qk_eps=g["qk_eps"], mlp_act=g["mlp_act"],
+                                  pos=g["pos"], inv_freq=g["inv_freq"], n_t=g["n_t"], n_h=g["n_h"],
+                                  linear=_block_linear(g, g["fmt"]), attn_fp32=False)
+        assert torch.equal(out, g["out"]), name
