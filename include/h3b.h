@@ -87,13 +87,18 @@ H3B_API int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t k, 
  * npu_quant_matmul with pertoken_scale, output_dtype bf16).
  * q: [m,k] int8, w: [n,k] int8 (the module's [N,K] weight, no transpose),
  * xs: [m] fp32, ws: [n] fp32, bias: [n] bf16 or NULL, y: [m,n] bf16 (row
- * stride ldy).  resid/gate are used by H3B_EPI_GATE_RES only (resid [m,n]
- * bf16 with row stride ldy, may alias y; gate [n] bf16).
+ * stride ldy).
+ * H3B_EPI_GATE_RES (the fused _mod_gate of model/dit.py:338-341):
+ * y[m,n] = resid[m,n] + v * gate[row_sel[m]*gate_ld + n]; resid is bf16 with
+ * row stride ldy and may alias y; row_sel (int32 [m]) may be NULL (row 0);
+ * rows with row_sel < 0 keep resid unchanged (tokens outside every segment).
+ * amax_out (optional, caller-zeroed fp32) receives max |y| over the output.
  * k % 128 == 0, n % 32 == 0, ldy % 8 == 0.
  */
 H3B_API int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* w, const float* ws, const void* bias,
-                     void* y, int64_t ldy, const void* resid, const void* gate, int epilogue, int64_t m,
-                     int64_t n, int64_t k, h3b_stream_t stream);
+                             void* y, int64_t ldy, const void* resid, const void* gate, int64_t gate_ld,
+                             const int32_t* row_sel, float* amax_out, int epilogue, int64_t m, int64_t n,
+                             int64_t k, h3b_stream_t stream);
 
 /*
  * Same GEMM, raw int32 accumulators acc[m,n] (row stride n) for bit-exact
@@ -144,10 +149,11 @@ H3B_API int h3b_nvfp4_swap_nibbles(const uint8_t* src, uint8_t* dst, int64_t nby
  * as well.  a_gs / w_gs: device fp32 scalars.  Other arguments as
  * h3b_gemm_i8_bf16.  k % 256 == 0, n % 32 == 0.
  */
-H3B_API int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs, const uint8_t* w_codes,
-                        const uint8_t* w_sf, const float* w_gs, const void* bias, void* y, int64_t ldy,
-                        const void* resid, const void* gate, int epilogue, int64_t m, int64_t n, int64_t k,
-                        h3b_stream_t stream);
+H3B_API int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs, const void* bias,
+                                void* y, int64_t ldy, const void* resid, const void* gate, int64_t gate_ld,
+                                const int32_t* row_sel, float* amax_out, int epilogue, int64_t m, int64_t n,
+                                int64_t k, h3b_stream_t stream);
 
 /* --------------------------------------------------------------- attention */
 
@@ -158,12 +164,14 @@ H3B_API int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, con
  * Element (s,h,d) of q lives at q + s*q_seq_stride + h*q_head_stride + d
  * (likewise k, v, o), so both the packed-QKV token-major layout [S,3,H,D]
  * and BNSD [H,S,D] are accepted without copies.  lse (optional, [heads, s_q]
- * fp32, natural log) receives the row log-sum-exp.  Replaces
+ * fp32, natural log) receives the row log-sum-exp; amax_out (optional,
+ * caller-zeroed fp32) receives max |o|.  Replaces
  * ops/fa_h3.py:224-304 (h3_attention_bnsd) and ops/attention.py:100-131
  * (fusion_attention_bnsd), whose host path is F.scaled_dot_product_attention.
  * Strides % 8 == 0, pointers 16-byte aligned.
  */
-H3B_API int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t heads,
+H3B_API int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, float* amax_out,
+                              int64_t heads,
                       int64_t s_q, int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
                       int64_t kv_seq_stride, int64_t kv_head_stride, int64_t o_seq_stride,
                       int64_t o_head_stride, float scale, h3b_stream_t stream);
@@ -186,25 +194,27 @@ H3B_API int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, int6
 /* ------------------------------------------------------- block elementwise */
 
 /*
- * h[r,:] = rmsnorm(x[r,:]) * w * (1 + scale_row) + shift_row, the fused
+ * h[r,:] = rmsnorm(x[r,:]) * w * (1 + scale_r) + shift_r: the fused
  * norm1/norm2 + _mod_scale_shift of model/dit.py:332-335,433-438 and
- * modules/linear.py:15-32.  Rows [seg_a, seg_b) use modulation row `row`
- * only; the caller issues one launch per (a, b, row) segment.  x, h: [m,
- * hidden] bf16 with row stride ld; w, shift, scale: [hidden] bf16 (shift and
- * scale point at the selected row).  Writes bf16 h, and when amax_out is not
- * NULL also atomically max-reduces |h| into amax_out[0] (which the caller
- * zeroes first) for the NVFP4 global scale.
+ * modules/linear.py:15-32, with the reference's bf16 rounding after each
+ * step.  shift_r = shift + row_sel[r]*tab_ld (likewise scale): the adaLN
+ * chunk tables of AdalnProj (model/dit.py:326-329) addressed in place;
+ * row_sel (int32 [m]) may be NULL (row 0); row_sel[r] < 0 leaves h = the
+ * plain RMSNorm (tokens outside every mod segment).  x, h: [m, hidden] bf16
+ * with row stride ld; w: [hidden] bf16.  amax_out (optional, caller-zeroed)
+ * receives max |h| for the NVFP4 global scale.
  */
 H3B_API int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidden, int64_t ld, const void* w,
-                         const void* shift, const void* scale, float eps, float* amax_out,
-                         h3b_stream_t stream);
+                                 const void* shift, const void* scale, int64_t tab_ld, const int32_t* row_sel,
+                                 float eps, float* amax_out, h3b_stream_t stream);
 
 /*
- * x[r,:] += y[r,:] * gate  (bf16, in place), the _mod_gate of
- * model/dit.py:338-341 for one segment.  gate: [hidden] bf16.
+ * x[r,:] += y[r,:] * gate_r  (bf16, in place), the _mod_gate of
+ * model/dit.py:338-341; gate_r = gate + row_sel[r]*tab_ld, rows with
+ * row_sel < 0 unchanged.
  */
 H3B_API int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidden, int64_t ld, const void* gate,
-                      h3b_stream_t stream);
+                              int64_t tab_ld, const int32_t* row_sel, h3b_stream_t stream);
 
 #ifdef __cplusplus
 }

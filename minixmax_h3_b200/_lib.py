@@ -20,20 +20,21 @@ SIGNATURES: dict[str, list] = {
     "h3b_version": [],
     "h3b_device_status": [c_ptr, c_int],
     "h3b_quant_i8_rows": [c_ptr, c_int, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr],
-    "h3b_gemm_i8_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_int, c_i64, c_i64, c_i64,
-                         c_ptr],
+    "h3b_gemm_i8_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_int,
+                         c_i64, c_i64, c_i64, c_ptr],
     "h3b_gemm_i8_acc_i32": [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr],
     "h3b_amax_bf16": [c_ptr, c_i64, c_ptr, c_ptr],
     "h3b_quant_nvfp4": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_ptr],
     "h3b_nvfp4_swap_nibbles": [c_ptr, c_ptr, c_i64, c_ptr],
-    "h3b_gemm_nvfp4_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_int,
-                            c_i64, c_i64, c_i64, c_ptr],
-    "h3b_attention_fwd": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
-                          c_i64, c_f32, c_ptr],
+    "h3b_gemm_nvfp4_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64,
+                            c_ptr, c_ptr, c_int, c_i64, c_i64, c_i64, c_ptr],
+    "h3b_attention_fwd": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                          c_i64, c_i64, c_f32, c_ptr],
     "h3b_qk_rmsnorm_rope": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_f32, c_ptr, c_i64, c_ptr,
                             c_int, c_int, c_ptr],
-    "h3b_rmsnorm_modulate": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_f32, c_ptr, c_ptr],
-    "h3b_gate_residual": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr],
+    "h3b_rmsnorm_modulate": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_f32, c_ptr,
+                             c_ptr],
+    "h3b_gate_residual": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr],
 }
 
 ERRORS = {
@@ -79,11 +80,18 @@ def lib() -> ctypes.CDLL:
     return _LIB
 
 
+# Entry points that launch no kernel of this library.
+_NO_LAUNCH = {"h3b_version", "h3b_device_status"}
+LAUNCHES = [0]  # kernels this process has launched through the ABI
+
+
 def call(name: str, *args) -> None:
     """Calls an entry point and raises H3bError on a non-zero status."""
     rc = getattr(lib(), name)(*args)
     if rc != 0:
         raise H3bError(name, rc)
+    if name not in _NO_LAUNCH:
+        LAUNCHES[0] += 1
 
 
 def device_status(clear: bool = True) -> tuple[int, int, int, int]:

@@ -59,6 +59,7 @@ constexpr size_t SMEM_BYTES = 1024 + 2 * TILE_BYTES + KST * TILE_BYTES + VST * T
 struct AttnArgs {
   __nv_bfloat16* o;
   float* lse;
+  float* amax_out;
   int64_t o_seq_stride;
   int64_t o_head_stride;
   int s_q;
@@ -321,6 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int q_row = q0 + wg * BQ + row;
       const float inv_l = 1.0f / l_run;
+      float o_amax = 0.0f;
       __nv_bfloat16* orow = args.o + static_cast<int64_t>(q_row) * args.o_seq_stride +
                             static_cast<int64_t>(head) * args.o_head_stride;
 #pragma unroll
@@ -337,8 +339,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             v.z = pack_bf16x2(__uint_as_float(r[e + 4]) * inv_l, __uint_as_float(r[e + 5]) * inv_l);
             v.w = pack_bf16x2(__uint_as_float(r[e + 6]) * inv_l, __uint_as_float(r[e + 7]) * inv_l);
             *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              o_amax = fmaxf(o_amax, fmaxf(fabsf(bf16lo_to_f32(w4[t])), fabsf(bf16hi_to_f32(w4[t]))));
           }
         }
+      }
+      if (args.amax_out != nullptr) {
+        const float wmax = warp_max(o_amax);
+        if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(args.amax_out), __float_as_uint(wmax));
       }
       if (args.lse != nullptr && q_row < args.s_q) {
         args.lse[static_cast<int64_t>(head) * args.s_q + q_row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
@@ -356,7 +366,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 }  // namespace
 
-extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t heads,
+extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, float* amax_out,
+                                 int64_t heads,
                                  int64_t s_q, int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
                                  int64_t kv_seq_stride, int64_t kv_head_stride, int64_t o_seq_stride,
                                  int64_t o_head_stride, float scale, h3b_stream_t stream) {
@@ -389,6 +400,7 @@ extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, vo
   AttnArgs a;
   a.o = static_cast<__nv_bfloat16*>(o);
   a.lse = lse;
+  a.amax_out = amax_out;
   a.o_seq_stride = o_seq_stride;
   a.o_head_stride = o_head_stride;
   a.s_q = static_cast<int>(s_q);

@@ -78,7 +78,8 @@ template <int MAXV>
 __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ h, int64_t m, int64_t hidden, int64_t ld,
     const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ shift,
-    const __nv_bfloat16* __restrict__ scale, float eps, float* __restrict__ amax_out) {
+    const __nv_bfloat16* __restrict__ scale, int64_t tab_ld, const int32_t* __restrict__ row_sel, float eps,
+    float* __restrict__ amax_out) {
   __shared__ float red[33];
   const int nvec = static_cast<int>(hidden >> 3);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,13 +113,17 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(red[32], static_cast<float>(hidden)) + eps));
   __syncthreads();  // red[] is reused by the next row
   __nv_bfloat16* hr = h + row * ld;
+  const int sel = row_sel != nullptr ? row_sel[row] : 0;
+  const bool modulate = sel >= 0;
+  const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
+  const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int vi = threadIdx.x + i * 256;
     if (vi < nvec) {
       const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
-      const uint4 sh = *reinterpret_cast<const uint4*>(shift + vi * 8);
-      const uint4 sc = *reinterpret_cast<const uint4*>(scale + vi * 8);
+      const uint4 sh = *reinterpret_cast<const uint4*>(shift_r + vi * 8);
+      const uint4 sc = *reinterpret_cast<const uint4*>(scale_r + vi * 8);
       const uint32_t xu[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
       const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
       const uint32_t shu[4] = {sh.x, sh.y, sh.z, sh.w};
@@ -134,7 +139,7 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
           const float shv = half ? bf16hi_to_f32(shu[e]) : bf16lo_to_f32(shu[e]);
           const float scv = half ? bf16hi_to_f32(scu[e]) : bf16lo_to_f32(scu[e]);
           const float nrm = bf16r(__fmul_rn(__fmul_rn(xv, rstd), wvv));
-          const float mod = bf16r(bf16r(nrm * bf16r(1.0f + scv)) + shv);
+          const float mod = modulate ? bf16r(bf16r(nrm * bf16r(1.0f + scv)) + shv) : nrm;
           amax = fmaxf(amax, fabsf(mod));
           o2[half] = mod;
         }
@@ -159,16 +164,19 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
 __global__ void __launch_bounds__(256) gate_residual_kernel(__nv_bfloat16* __restrict__ x,
                                                             const __nv_bfloat16* __restrict__ y, int64_t m,
                                                             int64_t hidden, int64_t ld,
-                                                            const __nv_bfloat16* __restrict__ gate) {
+                                                            const __nv_bfloat16* __restrict__ gate, int64_t tab_ld,
+                                                            const int32_t* __restrict__ row_sel) {
   const int64_t nvec_row = hidden >> 3;
   const int64_t total = m * nvec_row;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * 256) {
     const int64_t r = i / nvec_row, c = (i - r * nvec_row) * 8;
+    const int sel = row_sel != nullptr ? row_sel[r] : 0;
+    if (sel < 0) continue;  // token outside every mod segment: x unchanged
     uint4* xp = reinterpret_cast<uint4*>(x + r * ld + c);
     const uint4 xv = *xp;
     const uint4 yv = *reinterpret_cast<const uint4*>(y + r * ld + c);
-    const uint4 gv = *reinterpret_cast<const uint4*>(gate + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gate + static_cast<int64_t>(sel) * tab_ld + c);
     const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, yu[4] = {yv.x, yv.y, yv.z, yv.w},
                    gu[4] = {gv.x, gv.y, gv.z, gv.w};
     uint32_t o[4];
@@ -205,13 +213,13 @@ extern "C" int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, i
 }
 
 extern "C" int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidden, int64_t ld, const void* w,
-                                    const void* shift, const void* scale, float eps, float* amax_out,
-                                    h3b_stream_t stream) {
+                                    const void* shift, const void* scale, int64_t tab_ld, const int32_t* row_sel,
+                                    float eps, float* amax_out, h3b_stream_t stream) {
   if (x == nullptr || h == nullptr || w == nullptr || shift == nullptr || scale == nullptr) return H3B_ERR_ARG;
   if (m < 0 || hidden <= 0 || (hidden % 8) != 0 || ld < hidden || (ld % 8) != 0 || m > 0x7fffffff)
     return H3B_ERR_SHAPE;
   if (!h3b::aligned16(x) || !h3b::aligned16(h) || !h3b::aligned16(w) || !h3b::aligned16(shift) ||
-      !h3b::aligned16(scale))
+      !h3b::aligned16(scale) || tab_ld < 0 || (tab_ld % 8) != 0)
     return H3B_ERR_ALIGN;
   if (m == 0) return H3B_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -225,18 +233,21 @@ extern "C" int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t h
   if (blocks > m) blocks = m;
   const unsigned g = static_cast<unsigned>(blocks);
   if (nvec <= 256 * 2)
-    rmsnorm_modulate_kernel<2><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, eps, amax_out);
+    rmsnorm_modulate_kernel<2><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
+                                                  amax_out);
   else if (nvec <= 256 * 8)
-    rmsnorm_modulate_kernel<8><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, eps, amax_out);
+    rmsnorm_modulate_kernel<8><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
+                                                  amax_out);
   else
     return H3B_ERR_SHAPE;
   return h3b::launch_status();
 }
 
 extern "C" int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidden, int64_t ld, const void* gate,
-                                 h3b_stream_t stream) {
+                                 int64_t tab_ld, const int32_t* row_sel, h3b_stream_t stream) {
   if (x == nullptr || y == nullptr || gate == nullptr) return H3B_ERR_ARG;
   if (m < 0 || hidden <= 0 || (hidden % 8) != 0 || ld < hidden || (ld % 8) != 0) return H3B_ERR_SHAPE;
+  if (tab_ld < 0 || (tab_ld % 8) != 0) return H3B_ERR_ALIGN;
   if (!h3b::aligned16(x) || !h3b::aligned16(y) || !h3b::aligned16(gate)) return H3B_ERR_ALIGN;
   if (m == 0) return H3B_OK;
   int64_t blocks = (m * (hidden / 8) + 255) / 256;
@@ -244,6 +255,6 @@ extern "C" int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidd
   if (blocks > cap) blocks = cap;
   gate_residual_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), m, hidden, ld,
-      static_cast<const __nv_bfloat16*>(gate));
+      static_cast<const __nv_bfloat16*>(gate), tab_ld, row_sel);
   return h3b::launch_status();
 }

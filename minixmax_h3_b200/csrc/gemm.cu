@@ -46,7 +46,10 @@ struct GemmArgs {
   const uint8_t* w_sf; // nvf4: blocked scales of B
   const __nv_bfloat16* bias;
   const __nv_bfloat16* resid;
-  const __nv_bfloat16* gate;
+  const __nv_bfloat16* gate;  // [rows, gate_ld] adaLN gate table
+  const int32_t* row_sel;     // per output row: gate table row (NULL = 0, < 0 = keep resid)
+  float* amax_out;            // optional max |y|
+  int64_t gate_ld;
   void* y;
   int64_t ldy;
   int m, n, k;         // k in elements
@@ -236,6 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local % C::NACC;
@@ -246,6 +250,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int n0 = (tile % n_tiles) * BN;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.m;
+      int gate_row = 0;
+      if (args.epilogue == H3B_EPI_GATE_RES && args.row_sel != nullptr && row_ok) gate_row = args.row_sel[row];
+      const __nv_bfloat16* gate_r = args.gate + static_cast<int64_t>(gate_row < 0 ? 0 : gate_row) * args.gate_ld;
+      const float gmul = gate_row < 0 ? 0.0f : 1.0f;  // rows outside every segment keep resid
       float row_scale = 1.0f;
       if constexpr (KIND == KIND_I8) {
         if (args.out_mode == OUT_BF16 && row_ok) row_scale = args.xs[row];
@@ -298,20 +306,30 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              v[j + 2 * e] = __fadd_rn(bf16lo_to_f32(rw[e]),
-                                       __fmul_rn(v[j + 2 * e], __bfloat162float(args.gate[col0 + j + 2 * e])));
-              v[j + 2 * e + 1] = __fadd_rn(
-                  bf16hi_to_f32(rw[e]), __fmul_rn(v[j + 2 * e + 1], __bfloat162float(args.gate[col0 + j + 2 * e + 1])));
+              const float g0 = __bfloat162float(gate_r[col0 + j + 2 * e]) * gmul;
+              const float g1 = __bfloat162float(gate_r[col0 + j + 2 * e + 1]) * gmul;
+              v[j + 2 * e] = __fadd_rn(bf16lo_to_f32(rw[e]), __fmul_rn(v[j + 2 * e], g0));
+              v[j + 2 * e + 1] = __fadd_rn(bf16hi_to_f32(rw[e]), __fmul_rn(v[j + 2 * e + 1], g1));
             }
           }
         }
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
-          *reinterpret_cast<uint4*>(out + j) =
-              make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                         pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+          const uint4 pk = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                      pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+          *reinterpret_cast<uint4*>(out + j) = pk;
+          if (args.amax_out != nullptr) {
+            const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
+          }
         }
       }
+    }
+    if (args.amax_out != nullptr) {
+      y_amax = warp_max(y_amax);
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(args.amax_out), __float_as_uint(y_amax));
     }
   }
 
@@ -360,13 +378,14 @@ int check_common(int64_t m, int64_t n, int64_t k, int64_t kmul) {
 
 extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* w, const float* ws,
                                 const void* bias, void* y, int64_t ldy, const void* resid, const void* gate,
-                                int epilogue, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+                                int64_t gate_ld, const int32_t* row_sel, float* amax_out, int epilogue, int64_t m,
+                                int64_t n, int64_t k, h3b_stream_t stream) {
   if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr || y == nullptr) return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 128);
   if (rc != H3B_OK) return rc;
   if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
-  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr)) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
   if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(y)) return H3B_ERR_ALIGN;
   if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
   GemmArgs a{};
@@ -375,6 +394,9 @@ extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* 
   a.bias = static_cast<const __nv_bfloat16*>(bias);
   a.resid = static_cast<const __nv_bfloat16*>(resid);
   a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.gate_ld = gate_ld;
+  a.row_sel = row_sel;
+  a.amax_out = amax_out;
   a.y = y;
   a.ldy = ldy;
   a.m = static_cast<int>(m);
@@ -405,7 +427,8 @@ extern "C" int h3b_gemm_i8_acc_i32(const int8_t* q, const int8_t* w, int32_t* ac
 extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
                                    const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs,
                                    const void* bias, void* y, int64_t ldy, const void* resid, const void* gate,
-                                   int epilogue, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+                                   int64_t gate_ld, const int32_t* row_sel, float* amax_out, int epilogue,
+                                   int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
   if (a_codes == nullptr || a_sf == nullptr || a_gs == nullptr || w_codes == nullptr || w_sf == nullptr ||
       w_gs == nullptr || y == nullptr)
     return H3B_ERR_ARG;
@@ -414,7 +437,7 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
   if ((n % 128) != 0) return H3B_ERR_SHAPE;  // whole 128-row scale blocks for B
   if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
-  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr)) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
   if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(y) || !h3b::aligned16(a_sf) ||
       !h3b::aligned16(w_sf))
     return H3B_ERR_ALIGN;
@@ -427,6 +450,9 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
   a.bias = static_cast<const __nv_bfloat16*>(bias);
   a.resid = static_cast<const __nv_bfloat16*>(resid);
   a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.gate_ld = gate_ld;
+  a.row_sel = row_sel;
+  a.amax_out = amax_out;
   a.y = y;
   a.ldy = ldy;
   a.m = static_cast<int>(m);

@@ -58,17 +58,31 @@ def quant_i8_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def gemm_i8(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor,
             bias: Optional[torch.Tensor] = None, *, epilogue: int = EPI_STORE,
             resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+            row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
             out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = epi(acc * xs[m] * ws[n] + bias) in bf16; w is the [N, K] int8 weight."""
-    _cuda(q, xs, w, ws, bias, resid, gate, out)
+    """y = epi(acc * xs[m] * ws[n] + bias) in bf16; w is the [N, K] int8 weight.
+
+    EPI_GATE_RES: y = resid + v * gate[row_sel[m]] with gate a [rows, N] table
+    (a strided view is fine) and resid updated in place when out is None.
+    """
+    _cuda(q, xs, w, ws, bias, resid, gate, row_sel, amax_out, out)
     m, k = q.shape
     n = w.shape[0]
     if out is None:
-        out = resid if epilogue == EPI_GATE_RES and resid is not None and out is None else \
-            torch.empty((m, n), dtype=torch.bfloat16, device=q.device)
+        out = resid if epilogue == EPI_GATE_RES else torch.empty((m, n), dtype=torch.bfloat16, device=q.device)
+    gate_ld = _gate_ld(gate)
     call("h3b_gemm_i8_bf16", q.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), _ptr(bias), out.data_ptr(),
-         out.stride(0), _ptr(resid), _ptr(gate), epilogue, m, n, k, _stream(q))
+         out.stride(0), _ptr(resid), _ptr(gate), gate_ld, _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k,
+         _stream(q))
     return out
+
+
+def _gate_ld(gate: Optional[torch.Tensor]) -> int:
+    if gate is None:
+        return 0
+    if gate.stride(-1) != 1:
+        raise ValueError("gate table needs unit column stride")
+    return gate.stride(0) if gate.dim() == 2 else 0
 
 
 def gemm_i8_acc(q: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -137,18 +151,18 @@ def swap_nibbles(u8: torch.Tensor) -> torch.Tensor:
 
 def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = None, *,
                epilogue: int = EPI_STORE, resid: Optional[torch.Tensor] = None,
-               gate: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               gate: Optional[torch.Tensor] = None, row_sel: Optional[torch.Tensor] = None,
+               amax_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = epi(a_gs*w_gs * A @ W^T + bias) in bf16; both operands lo-first."""
     if a.hi_first or w.hi_first:
         raise ValueError("gemm_nvfp4 needs tensor-core (lo-first) nibble order; repack with swap_nibbles")
-    _cuda(a.codes, w.codes, bias, resid, gate, out)
+    _cuda(a.codes, w.codes, bias, resid, gate, row_sel, amax_out, out)
     m, n, k = a.rows, w.rows, a.k
     if out is None:
-        out = resid if epilogue == EPI_GATE_RES and resid is not None else \
-            torch.empty((m, n), dtype=torch.bfloat16, device=a.codes.device)
+        out = resid if epilogue == EPI_GATE_RES else torch.empty((m, n), dtype=torch.bfloat16, device=a.codes.device)
     call("h3b_gemm_nvfp4_bf16", a.codes.data_ptr(), a.sf.data_ptr(), a.gs.data_ptr(), w.codes.data_ptr(),
          w.sf.data_ptr(), w.gs.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0), _ptr(resid), _ptr(gate),
-         epilogue, m, n, k, _stream(a.codes))
+         _gate_ld(gate), _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k, _stream(a.codes))
     return out
 
 
@@ -156,13 +170,14 @@ def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = No
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
-              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+              amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Non-causal attention over token-major views q [Sq,H,128], k/v [Skv,H,128].
 
     Any strides with a unit last dimension are accepted (e.g. slices of a packed
     [S, 3, H, D] QKV buffer).  Returns o [Sq, H, 128] bf16.
     """
-    _cuda(q, k, v, out, lse)
+    _cuda(q, k, v, out, lse, amax_out)
     for t in (q, k, v):
         if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[-1] != 128 or t.stride(-1) != 1:
             raise ValueError("attention expects bf16 [S, H, 128] views with unit last stride")
@@ -173,7 +188,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optio
     if out is None:
         out = torch.empty((s_q, heads, d), dtype=torch.bfloat16, device=q.device)
     scale = d ** -0.5 if scale is None else float(scale)
-    call("h3b_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse), heads, s_q,
+    call("h3b_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse), _ptr(amax_out),
+         heads, s_q,
          s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), out.stride(0), out.stride(1), scale, _stream(q))
     return out
 
@@ -194,18 +210,30 @@ def qk_rmsnorm_rope(q: torch.Tensor, k: Optional[torch.Tensor], q_weight: torch.
 
 
 def rmsnorm_modulate(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float,
-                     out: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    _cuda(x, weight, shift, scale, out, amax_out)
+                     row_sel: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                     amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """h = rmsnorm(x)*w*(1+scale[row_sel]) + shift[row_sel]; shift/scale are
+    [rows, hidden] tables (strided views of the adaLN output are fine)."""
+    _cuda(x, weight, shift, scale, row_sel, out, amax_out)
     x2, m, hidden, ld = _rows(x)
     if out is None:
         out = torch.empty((m, hidden), dtype=torch.bfloat16, device=x.device)
+    if shift.stride() != scale.stride():
+        raise ValueError("shift and scale tables must share strides")
+    if out.stride(0) != ld:
+        raise ValueError("out must share the row stride of x")
     call("h3b_rmsnorm_modulate", x2.data_ptr(), out.data_ptr(), m, hidden, ld, weight.data_ptr(), shift.data_ptr(),
-         scale.data_ptr(), eps, _ptr(amax_out), _stream(x))
+         scale.data_ptr(), _gate_ld(shift), _ptr(row_sel), eps, _ptr(amax_out), _stream(x))
     return out
 
 
-def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
-    _cuda(x, y, gate)
+def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
+                  row_sel: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x += y * gate[row_sel] in place (bf16)."""
+    _cuda(x, y, gate, row_sel)
     m, hidden = x.shape
-    call("h3b_gate_residual", x.data_ptr(), y.data_ptr(), m, hidden, x.stride(0), gate.data_ptr(), _stream(x))
+    if y.stride() != x.stride():
+        raise ValueError("x and y must share strides")
+    call("h3b_gate_residual", x.data_ptr(), y.data_ptr(), m, hidden, x.stride(0), gate.data_ptr(), _gate_ld(gate),
+         _ptr(row_sel), _stream(x))
     return x

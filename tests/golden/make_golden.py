@@ -82,6 +82,8 @@ def make_attention(R) -> dict:
 
 
 def block_params(g: torch.Generator, hidden: int, heads: int, ffn_out: int, ffn_in: int, t_dim: int) -> dict:
+    """Seeded block weights (bf16).  The fixtures store only the seed; tests
+    call this again with the same generator state to rebuild them."""
     inner = heads * 128
     p = {
         "qkv_w": torch.randn(3 * inner, hidden, generator=g) * 0.02,
@@ -98,20 +100,32 @@ def block_params(g: torch.Generator, hidden: int, heads: int, ffn_out: int, ffn_
     return {k: v.to(torch.bfloat16) for k, v in p.items()}
 
 
-def make_block(R, fmt: str, mlp_act: str) -> dict:
+BLOCK_CFG = {"hidden": 256, "heads": 2, "t_dim": 32, "eps": 1e-6, "qk_eps": 1e-6, "grid": (1, 8, 16)}
+
+
+def block_fixture_params(fix: dict) -> dict:
+    """Rebuilds the weights of a block fixture from its seed."""
+    g = torch.Generator().manual_seed(fix["seed"])
+    hidden, ffn = fix["hidden"], 4 * fix["hidden"]
+    ffn_out = ffn if fix["mlp_act"] == "gelu" else 2 * ffn
+    return block_params(g, hidden, fix["heads"], ffn_out, ffn, fix["t_dim"])
+
+
+def make_block(R, fmt: str, mlp_act: str, seed: int = 4) -> dict:
     """Reference DiTBlock with its four projections swapped for the oracle's
     emulated quantised linear (the only part the reference cannot run on CPU)."""
-    g = torch.Generator().manual_seed(4)
-    hidden, heads, t_dim, eps, qk_eps = 128, 1, 32, 1e-6, 1e-6
-    grid = (1, 8, 8)
+    c = BLOCK_CFG
+    hidden, heads, t_dim, eps, qk_eps, grid = c["hidden"], c["heads"], c["t_dim"], c["eps"], c["qk_eps"], c["grid"]
     s_len = grid[0] * grid[1] * grid[2]
     ffn = 4 * hidden
-    ffn_out = ffn if mlp_act == "gelu" else 2 * ffn
-    p = block_params(g, hidden, heads, ffn_out, ffn, t_dim)
+    fix = {"seed": seed, "fmt": fmt, "mlp_act": mlp_act, "hidden": hidden, "heads": heads, "t_dim": t_dim,
+           "eps": eps, "qk_eps": qk_eps, "grid": grid}
+    p = block_fixture_params(fix)
+    g = torch.Generator().manual_seed(seed + 1000)
     x = torch.randn(s_len, hidden, generator=g).to(torch.bfloat16)
     t = torch.rand(1, generator=g) * 1000.0
     t_emb = O.timestep_embedding(t, t_dim).to(torch.bfloat16)
-    segments = [(0, s_len // 4, 1), (s_len // 4, s_len, 0)]
+    segments = [(0, s_len // 4, 1), (s_len // 4, s_len - 8, 0)]  # last 8 tokens: in no segment
 
     blk = R.dit.DiTBlock(hidden, heads, 128, ffn, t_dim, eps, qk_eps, apply_silu=True, dtype=torch.bfloat16)
     blk.norm1.weight.data.copy_(p["norm1_w"])
@@ -133,9 +147,9 @@ def make_block(R, fmt: str, mlp_act: str) -> dict:
     table = R.rope.rope_rotation_table(O.rope_angles(pos, inv, 22, 21), torch.bfloat16)
     with torch.no_grad():
         out = blk(x.clone(), t_emb, segments, table)
-    return {"fmt": fmt, "mlp_act": mlp_act, "hidden": hidden, "heads": heads, "t_dim": t_dim, "eps": eps,
-            "qk_eps": qk_eps, "grid": grid, "segments": segments, "params": p, "x": x, "t_emb": t_emb,
-            "pos": pos, "inv_freq": inv, "n_t": 22, "n_h": 21, "out": out}
+    fix.update({"segments": segments, "x": x, "t_emb": t_emb, "pos": pos, "inv_freq": inv, "n_t": 22, "n_h": 21,
+                "out": out})
+    return fix
 
 
 def main() -> None:

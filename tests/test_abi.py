@@ -32,11 +32,14 @@ def test_library_exports_every_symbol():
 
 @pytest.mark.parametrize("name,args,code", [
     ("h3b_quant_i8_rows", (None, 0, 4, 64, 64, None, None, None), 8),
-    ("h3b_gemm_i8_bf16", (1, 1, 1, 1, None, 1, 64, None, None, 0, 4, 48, 128, None), 1),   # n % 32
-    ("h3b_gemm_i8_bf16", (1, 1, 1, 1, None, 1, 64, None, None, 0, 4, 64, 100, None), 1),   # k % 128
-    ("h3b_gemm_nvfp4_bf16", (16, 16, 16, 16, 16, 16, None, 16, 256, None, None, 0, 4, 256, 128, None), 1),
+    ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 0, 4, 48, 128, None), 1),  # n%32
+    ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 0, 4, 64, 100, None), 1),  # k%128
+    ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 2, 4, 64, 128, None), 8),  # gate
+    ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 256, None, None, 0, None, None, 0, 4, 256, 128, None), 1),
     ("h3b_quant_nvfp4", (16, 4, 48, 48, 16, 16, 16, 16, 1, None), 1),                       # k % 64
-    ("h3b_attention_fwd", (None,) * 5 + (1, 1, 1, 128, 128, 128, 128, 128, 128, 0.1, None), 8),
+    ("h3b_attention_fwd", (None,) * 6 + (1, 1, 1, 128, 128, 128, 128, 128, 128, 0.1, None), 8),
+    ("h3b_attention_fwd", (16,) * 4 + (None, None, 1, 1, 1, 100, 128, 128, 128, 128, 128, 0.1, None), 2),
+    ("h3b_rmsnorm_modulate", (16, 16, 4, 100, 100, 16, 16, 16, 0, None, 1e-6, None, None), 1),
     ("h3b_amax_bf16", (16, 7, 16, None), 1),
 ])
 def test_host_side_validation(name, args, code):

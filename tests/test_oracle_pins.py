@@ -137,16 +137,19 @@ def test_ulysses_layout_matches_reference_permutation():
         assert torch.equal(got, O.seq_to_head_local(full, ws, r))
 
 
-def _block_linear(g, fmt):
-    lin = {n: O.EmulatedQuantLinear(g["params"][f"{n}_w"], fmt) for n in ("qkv", "out", "fc1", "fc2")}
+def _block_linear(params, fmt):
+    lin = {n: O.EmulatedQuantLinear(params[f"{n}_w"], fmt) for n in ("qkv", "out", "fc1", "fc2")}
     return lambda name, x: lin[name](x)
 
 
 def test_dit_block_golden_bit_exact():
+    from golden.make_golden import block_fixture_params
+
     for name in ("dit_block_int8_gelu.pt", "dit_block_nvfp4_gelu.pt", "dit_block_nvfp4_swiglu.pt"):
         g = load_golden(name)
-        out = O.dit_block_forward(g["x"].clone(), g["t_emb"], g["segments"], g["params"], heads=g["heads"],
+        params = block_fixture_params(g)
+        out = O.dit_block_forward(g["x"].clone(), g["t_emb"], g["segments"], params, heads=g["heads"],
                                   head_dim=128, eps=g["eps"], qk_eps=g["qk_eps"], mlp_act=g["mlp_act"],
                                   pos=g["pos"], inv_freq=g["inv_freq"], n_t=g["n_t"], n_h=g["n_h"],
-                                  linear=_block_linear(g, g["fmt"]), attn_fp32=False)
+                                  linear=_block_linear(params, g["fmt"]), attn_fp32=False)
         assert torch.equal(out, g["out"]), name

@@ -1,0 +1,99 @@
+"""CPU, world_size 2/4 over gloo: the Ulysses exchanges of
+minixmax_h3_b200.ulysses reproduce the reference's layout (ops/ulysses.py)
+bit-for-bit, and a rank that dies is reported by the others as an error."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=20))
+        from minixmax_h3_b200 import dist as hdist
+        from minixmax_h3_b200 import ulysses as U
+        from oracle import h3_oracle as O
+
+        hdist.set_state(rank, ws, group=dist.group.WORLD, backend="gloo")
+        s, h, d = 6 * ws, 2 * ws, 4
+        full = torch.arange(s * h * d, dtype=torch.float32).reshape(s, h, d)
+        s0, s1 = U.split_range(s)
+        assert (s0, s1) == O.split_range(s, ws, rank)
+        local = full[s0:s1].contiguous()
+        if mode == "exchange":
+            got = U.all_to_all_heads(local, gather_seq=True)
+            assert torch.equal(got, O.seq_to_head_local(full, ws, rank))
+            back = U.all_to_all_heads(got, gather_seq=False)
+            assert torch.equal(back, local)
+            qkv_full = torch.randn(s, 3, h, d, generator=torch.Generator().manual_seed(1))
+            tq, tk, tv = U.all_to_all_qkv(qkv_full[s0:s1].reshape(s1 - s0, -1).contiguous(), h, d)
+            for t, part in ((tq, 0), (tk, 1), (tv, 2)):
+                assert torch.equal(t, O.seq_to_head_local(qkv_full[:, part], ws, rank))
+            segs = [(0, 5, 1), (5, s, 0)]
+            assert U.clip_mod_segments(segs, s0, s1) == O.clip_mod_segments(segs, s0, s1)
+            results.put((rank, "ok"))
+        elif mode == "dead_peer":
+            U.all_to_all_heads(local, gather_seq=True)  # a healthy step: connections are up
+            if rank == ws - 1:
+                results.put((rank, "exited"))
+                results.close()
+                results.join_thread()  # flush before the hard exit
+                os._exit(0)  # leaves between steps, nothing in flight
+            try:
+                U.all_to_all_heads(local, gather_seq=True)
+                results.put((rank, "no error"))
+            except Exception as e:  # noqa: BLE001 - any transport error is the expected outcome
+                results.put((rank, f"error:{type(e).__name__}"))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        results.put((rank, f"fail:{e!r}"))
+
+
+def _run(ws: int, mode: str, timeout: float = 120.0) -> dict:
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, mode, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(ws):
+            r, msg = q.get(timeout=timeout)
+            out[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return out
+
+
+@pytest.mark.parametrize("ws", [2, 4])
+def test_ulysses_exchanges_match_reference_layout(ws):
+    res = _run(ws, "exchange")
+    assert res == {r: "ok" for r in range(ws)}, res
+
+
+def test_dead_peer_is_reported_not_hung():
+    res = _run(2, "dead_peer")
+    assert res[1] == "exited"
+    assert res[0].startswith("error:"), res
