@@ -276,7 +276,8 @@ def run_gpu(args) -> None:
         ATTN_TIMER.enabled = False
         attn = ATTN_TIMER.drain()
         launches = _lib.LAUNCHES[0] - launches0
-    compute_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    step_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    compute_ms = sum(step_ms) / args.steps
     e2e_ms = sum(e[0].elapsed_time(e[3]) for e in ev) / args.steps
     t = torch.tensor([compute_ms, e2e_ms], device=dev)
     if ws > 1:
@@ -316,6 +317,7 @@ def run_gpu(args) -> None:
             "cpu_baseline": cpu,
             "clocks": clock,
             "gpu_launches": launches,
+            "step_ms": [round(v, 1) for v in step_ms],
         }
         print(json.dumps(line), flush=True)
     if ws > 1:

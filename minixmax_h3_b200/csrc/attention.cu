@@ -11,14 +11,22 @@
 //   warp 8      TMA producer: Q0/Q1 once, K and V through 2-deep rings
 //   warp 9      TMEM allocator + single-thread MMA issuer
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each.  The softmax
-// writes P as packed bf16 into the first 64 columns of its S region and the
-// P.V product reads it straight from TMEM (tcgen05.mma with the A operand in
-// TMEM), so P never touches shared memory.  The row max is rescaled lazily:
-// O and the row sum are corrected only when the running max grows by more
-// than 8 (log2 domain), which bounds P by 2^8.
+// writes P as packed bf16 into the first 64 columns of the S region it read,
+// and P.V reads it straight from TMEM (tcgen05.mma with the A operand in
+// TMEM), so P never touches shared memory.
+// MMA issue order: S0(0) S1(0) PV0(0), then per K/V tile j >= 1:
+//   S0(j)  PV1(j-1)  S1(j)  PV0(j)        (and PV1(n-1) at the end)
+// so the tensor pipe always holds the other tile's work while a softmax runs.
+// S_i(j) is issued right behind PV_i(j-1), which reads P_i(j-1) from the same
+// columns: the tcgen05.mma stream of one thread executes in order, so the
+// write cannot overtake the read.  The commit after S_i(j) also covers
+// PV_i(j-1), so when a softmax sees S_i(j) ready, O_i is settled.
+// The row max is rescaled lazily: O and the row sum are corrected only when
+// the running max grows by more than 8 (log2 domain), which bounds P by 2^8.
 // Q/K tiles are K-major and V tiles MN-major, all with the 128-byte swizzle,
 // loaded by non-multicast TMA from any (seq, head) strides.  Every wait is
-// bounded.
+// bounded, and every parity wait is at most one phase behind its barrier
+// (the argument is given at each wait).
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
 
@@ -32,13 +40,19 @@ constexpr int BQ = 128;    // rows per Q tile (one softmax warpgroup)
 constexpr int BKV = 128;   // rows per K/V tile
 constexpr int KST = 2;     // K ring depth
 constexpr int VST = 2;     // V ring depth
-constexpr int TILE_BYTES = 128 * D * 2;  // 32 KB: two 16 KB swizzle boxes (d 0-63, 64-127)
-constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int Q_TILE_BYTES = BQ * D * 2;        // 32 KB: two 16 KB boxes (d 0-63, 64-127)
+constexpr int Q_HALF_BYTES = Q_TILE_BYTES / 2;
+constexpr int KV_TILE_BYTES = BKV * D * 2;      // 32 KB: two 16 KB boxes
+constexpr int KV_HALF_BYTES = KV_TILE_BYTES / 2;
 constexpr int THREADS = 320;
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 constexpr uint32_t IDESC_S = idesc_bf16_f32(128, BKV, 0, 0);  // Q (K-major) x K^T (K-major)
 constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, 0, 1);    // P (TMEM) x V (MN-major)
+
+// TMEM column of S_i (P_i in its first 64 columns) and of O_i.
+__host__ __device__ constexpr uint32_t s_col(int i) { return static_cast<uint32_t>(i * 128); }
+__host__ __device__ constexpr uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 128); }
 
 struct __align__(8) Bars {
   uint64_t q_full;
@@ -46,15 +60,15 @@ struct __align__(8) Bars {
   uint64_t k_empty[KST];
   uint64_t v_full[VST];
   uint64_t v_empty[VST];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
+  uint64_t s_full[2];      // [tile]: S_i(j) ready (tcgen05.commit)
+  uint64_t p_full[2];      // [tile]: P_i(j) written (128 softmax threads)
+  uint64_t pv_done[2];     // [tile]: O_i += P_i(j) V_j complete (tcgen05.commit)
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + 2 * TILE_BYTES + KST * TILE_BYTES + VST * TILE_BYTES + sizeof(Bars);
+constexpr size_t SMEM_BYTES = 1024 + 2 * Q_TILE_BYTES + KST * KV_TILE_BYTES + VST * KV_TILE_BYTES + sizeof(Bars);
 
 struct AttnArgs {
   __nv_bfloat16* o;
@@ -79,15 +93,45 @@ H3B_DEV float fast_exp2(float x) {
   return y;
 }
 
+// Row max of one 64-column S tile with 8 independent chains (MASK: columns
+// >= valid of the last K/V tile are padding).
+template <bool MASK>
+H3B_DEV float row_max64(const uint32_t* r, int valid) {
+  float mx[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx[e] = (!MASK || e < valid) ? __uint_as_float(r[e]) : -INFINITY;
+#pragma unroll
+  for (int e = 8; e < 64; ++e) mx[e & 7] = fmaxf(mx[e & 7], (!MASK || e < valid) ? __uint_as_float(r[e]) : -INFINITY);
+  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+}
+
+// p = exp2(s*scale_log2 - m) for 64 columns: summed in 4 chains, packed to
+// 32 bf16 pairs.
+template <bool MASK>
+H3B_DEV float exp_pack64(const uint32_t* r, int valid, float scale_log2, float neg_m, uint32_t (&pk)[32]) {
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const float sa = (!MASK || 2 * e < valid) ? __uint_as_float(r[2 * e]) : -INFINITY;
+    const float sb = (!MASK || 2 * e + 1 < valid) ? __uint_as_float(r[2 * e + 1]) : -INFINITY;
+    const float a = fast_exp2(fmaf(sa, scale_log2, neg_m));
+    const float b = fast_exp2(fmaf(sb, scale_log2, neg_m));
+    acc[e & 3] += a + b;
+    pk[e] = pack_bf16x2(a, b);
+  }
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// 10 warps: two SM sub-partitions host 3 warps, capping registers at 168.
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                           // Q0 | Q1
-  uint8_t* sK = sQ + 2 * TILE_BYTES;            // K ring
-  uint8_t* sV = sK + KST * TILE_BYTES;          // V ring
-  Bars* bars = reinterpret_cast<Bars*>(sV + VST * TILE_BYTES);
+  uint8_t* sQ = smem;                            // Q0 | Q1
+  uint8_t* sK = sQ + 2 * Q_TILE_BYTES;           // K ring
+  uint8_t* sV = sK + KST * KV_TILE_BYTES;        // V ring
+  Bars* bars = reinterpret_cast<Bars*>(sV + VST * KV_TILE_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -130,30 +174,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
+      mbar_arrive_expect_tx(&bars->q_full, 2 * Q_TILE_BYTES);
       for (int t = 0; t < 2; ++t)
         for (int h = 0; h < 2; ++h)
-          tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tm_q, h * 64, q0 + t * BQ, head, &bars->q_full);
+          tma_load_3d(sQ + t * Q_TILE_BYTES + h * Q_HALF_BYTES, &tm_q, h * 64, q0 + t * BQ, head,
+                      &bars->q_full);
       bool ok = true;
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_kv && ok; ++j) {
+        // Slot j%KST was last used by K_{j-KST}; its release is phase j/KST-1.
         const int ks = j % KST;
         if (j >= KST && !mbar_wait(&bars->k_empty[ks], ((j / KST) - 1) & 1, &g_status, 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&bars->k_full[ks], TILE_BYTES);
+        mbar_arrive_expect_tx(&bars->k_full[ks], KV_TILE_BYTES);
         for (int h = 0; h < 2; ++h)
-          tma_load_3d(sK + ks * TILE_BYTES + h * HALF_BYTES, &tm_k, h * 64, j * BKV, head, &bars->k_full[ks]);
+          tma_load_3d(sK + ks * KV_TILE_BYTES + h * KV_HALF_BYTES, &tm_k, h * 64, j * BKV, head,
+                      &bars->k_full[ks]);
         issued_k = j + 1;
         const int vs = j % VST;
         if (j >= VST && !mbar_wait(&bars->v_empty[vs], ((j / VST) - 1) & 1, &g_status, 2, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&bars->v_full[vs], TILE_BYTES);
+        mbar_arrive_expect_tx(&bars->v_full[vs], KV_TILE_BYTES);
         for (int h = 0; h < 2; ++h)
-          tma_load_3d(sV + vs * TILE_BYTES + h * HALF_BYTES, &tm_v, h * 64, j * BKV, head, &bars->v_full[vs]);
+          tma_load_3d(sV + vs * KV_TILE_BYTES + h * KV_HALF_BYTES, &tm_v, h * 64, j * BKV, head,
+                      &bars->v_full[vs]);
         issued_v = j + 1;
       }
       if (!ok || *abort_flag) {
@@ -170,58 +218,74 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       bool ok = mbar_wait(&bars->q_full, 0, &g_status, 3, abort_flag);
       tc_fence_after();
-      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + TILE_BYTES)};
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int ks = j % KST;
-        if (!mbar_wait(&bars->k_full[ks], (j / KST) & 1, &g_status, 4, abort_flag)) {
-          ok = false;
-          break;
-        }
+      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + Q_TILE_BYTES)};
+      auto wait_k = [&](int j) -> uint32_t {
+        if (!mbar_wait(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return 0u;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + ks * TILE_BYTES);
-        for (int i = 0; i < 2 && ok; ++i) {
-          // S_i aliases P_i of the previous tile: wait until P_i.V has run.
-          if (j > 0 && !mbar_wait(&bars->pv_done[i], (j - 1) & 1, &g_status, 5, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t s_tmem = tmem + i * 128;
+        return smem_u32(sK + (j % KST) * KV_TILE_BYTES);
+      };
+      auto wait_v = [&](int j) -> uint32_t {
+        if (!mbar_wait(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return 0u;
+        tc_fence_after();
+        return smem_u32(sV + (j % VST) * KV_TILE_BYTES);
+      };
+      // S_i = Q_i K^T (fresh accumulator), then publish it.
+      auto issue_s = [&](int i, uint32_t k_addr) {
+        const uint32_t d = tmem + s_col(i);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * HALF_BYTES;
-            const uint64_t ad = sdesc_kmajor_sw128(q_addr[i] + off) + (kk & 3) * 2;
-            const uint64_t bd = sdesc_kmajor_sw128(k_addr + off) + (kk & 3) * 2;
-            mma_f16_ss(s_tmem, ad, bd, IDESC_S, kk > 0);
-          }
-          tc_commit(&bars->s_full[i]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = sdesc_kmajor_sw128(q_addr[i] + (kk >> 2) * Q_HALF_BYTES) + (kk & 3) * 2;
+          const uint64_t bd = sdesc_kmajor_sw128(k_addr + (kk >> 2) * KV_HALF_BYTES) + (kk & 3) * 2;
+          mma_f16_ss(d, ad, bd, IDESC_S, kk > 0);
         }
-        if (!ok) break;
-        tc_commit(&bars->k_empty[ks]);
-        const int vs = j % VST;
-        if (!mbar_wait(&bars->v_full[vs], (j / VST) & 1, &g_status, 6, abort_flag)) {
+        tc_commit(&bars->s_full[i]);
+      };
+      // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  p_full[i]
+      // completes once per tile; the softmax cannot arrive for j+1 before
+      // S_i(j+1), which is issued after this wait, so it is one phase behind.
+      auto issue_pv = [&](int i, int j, uint32_t v_addr) -> bool {
+        if (!mbar_wait(&bars->p_full[i], j & 1, &g_status, 7, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t p_tmem = tmem + s_col(i);
+        const uint32_t o_tmem = tmem + o_col(i);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t bd = sdesc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF_BYTES, 1024);
+          mma_f16_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&bars->pv_done[i]);
+        return true;
+      };
+      uint32_t k_addr = ok ? wait_k(0) : 0u;
+      ok = k_addr != 0u;
+      if (ok) {
+        issue_s(0, k_addr);
+        issue_s(1, k_addr);
+        tc_commit(&bars->k_empty[0]);
+      }
+      uint32_t v_prev = ok ? wait_v(0) : 0u;
+      ok = ok && v_prev != 0u && issue_pv(0, 0, v_prev);
+      for (int j = 1; j < n_kv && ok; ++j) {
+        k_addr = wait_k(j);
+        if (k_addr == 0u) {
           ok = false;
           break;
         }
-        const uint32_t v_addr = smem_u32(sV + vs * TILE_BYTES);
-        for (int i = 0; i < 2 && ok; ++i) {
-          if (!mbar_wait(&bars->p_full[i], j & 1, &g_status, 7, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t p_tmem = tmem + i * 128;
-          const uint32_t o_tmem = tmem + 256 + i * 128;
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint64_t bd = sdesc_mnmajor_sw128(v_addr + kk * 2048, HALF_BYTES, 1024);
-            mma_f16_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&bars->pv_done[i]);
+        issue_s(0, k_addr);                       // behind PV0(j-1) in the pipe
+        if (!issue_pv(1, j - 1, v_prev)) {        // PV1(j-1)
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        tc_commit(&bars->v_empty[vs]);
+        tc_commit(&bars->v_empty[(j - 1) % VST]);  // V_{j-1} fully consumed
+        issue_s(1, k_addr);                       // behind PV1(j-1)
+        tc_commit(&bars->k_empty[j % KST]);
+        v_prev = wait_v(j);
+        if (v_prev == 0u || !issue_pv(0, j, v_prev)) {
+          ok = false;
+          break;
+        }
       }
+      if (ok && issue_pv(1, n_kv - 1, v_prev)) tc_commit(&bars->v_empty[(n_kv - 1) % VST]);
       tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
     }
@@ -231,51 +295,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;          // row within the Q tile
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t s_tmem = tmem + wg * 128 + lane_off;
-    const uint32_t o_tmem = tmem + 256 + wg * 128 + lane_off;
+    const uint32_t o_tmem = tmem + o_col(wg) + lane_off;
     float m_run = -INFINITY;  // running max, log2 domain (already scaled)
     float l_run = 0.0f;
     bool ok = true;
+    const uint32_t s_tmem = tmem + s_col(wg) + lane_off;
     for (int j = 0; j < n_kv; ++j) {
+      // s_full[wg] completes once per tile; the MMA cannot publish S(j+1)
+      // before P(j) is written below, so this wait is one phase behind.
       if (!warp_wait(&bars->s_full[wg], j & 1, 20, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_tmem + c * 32, r);
-        tc_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
-      }
       const int valid = args.s_kv - j * BKV;  // columns >= valid are padding
-      if (valid < BKV) {
+      const bool full = valid >= BKV;
+      // Pass 1: row max over two 64-column halves.
+      float row_max = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 128; ++e)
-          if (e >= valid) s[e] = -INFINITY;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[64];
+        tmem_ld32p(s_tmem + h * 64, r);
+        tmem_ld32p(s_tmem + h * 64 + 32, r + 32);
+        tmem_wait_fence<2>(r);
+        const float m = full ? row_max64<false>(r, valid - h * 64) : row_max64<true>(r, valid - h * 64);
+        row_max = fmaxf(row_max, m);
       }
-      float mx = s[0];
-#pragma unroll
-      for (int e = 1; e < 128; ++e) mx = fmaxf(mx, s[e]);
-      const float m_tile = mx * args.scale_log2;
+      const float m_tile = row_max * args.scale_log2;
       float m_use = m_run;
       bool rescale = false;
       if (m_tile > m_run + RESCALE_THRESHOLD) {
         m_use = m_tile;
         rescale = true;
-      }
-      const float neg_m = -m_use;
-      float sum = 0.0f;
-      uint32_t p[64];
-#pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const float a = fast_exp2(fmaf(s[2 * e], args.scale_log2, neg_m));
-        const float b = fast_exp2(fmaf(s[2 * e + 1], args.scale_log2, neg_m));
-        sum += a + b;
-        p[e] = pack_bf16x2(a, b);
       }
       // The correction runs warp-uniformly: tcgen05.ld/st are .sync.aligned
       // and warp_wait shuffles over the full warp, so a per-row branch here
@@ -284,7 +335,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float factor = rescale ? fast_exp2(m_run - m_use) : 1.0f;  // 0 on the first tile
         l_run = l_run * factor;
         if (j > 0) {
-          // O_i holds P.V of tiles < j: wait for the last one, then scale it.
+          // O_i holds P.V of tiles < j.  The commit that published S_i(j)
+          // already covered PV_i(j-1); the wait (phase j-1, with phase j-2
+          // complete before S_i(j-1) was read) only formalises that.
           if (!warp_wait(&bars->pv_done[wg], (j - 1) & 1, 21, abort_flag)) {
             ok = false;
             break;
@@ -292,33 +345,38 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(o_tmem + c * 32, r);
-            tc_wait_ld();
+            uint32_t o[32];
+            tmem_ld32p(o_tmem + c * 32, o);
+            tmem_wait_fence<1>(o);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
-            tmem_st32(o_tmem + c * 32, r);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st32(o_tmem + c * 32, o);
           }
         }
         if (rescale) m_run = m_use;
       }
-      l_run += sum;
-      {
-        uint32_t lo[32], hi[32];
+      // Pass 2: P = exp2(s*scale - m) as packed bf16.  P half h covers columns
+      // 32h..32h+31, which overlap only S columns already loaded.
+      float sum = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          lo[e] = p[e];
-          hi[e] = p[32 + e];
-        }
-        tmem_st32(s_tmem, lo);
-        tmem_st32(s_tmem + 32, hi);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[64];
+        tmem_ld32p(s_tmem + h * 64, r);
+        tmem_ld32p(s_tmem + h * 64 + 32, r + 32);
+        tmem_wait_fence<2>(r);
+        uint32_t pk[32];
+        sum += full ? exp_pack64<false>(r, valid - h * 64, args.scale_log2, -m_use, pk)
+                    : exp_pack64<true>(r, valid - h * 64, args.scale_log2, -m_use, pk);
+        tmem_st32(s_tmem + h * 32, pk);
       }
+      l_run += sum;
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_full[wg]);
     }
-    // ---- epilogue: O / l -> bf16 rows
-    if (ok && warp_wait(&bars->pv_done[wg], (n_kv - 1) & 1, 22, abort_flag)) {
+    // ---- epilogue: O / l -> bf16 rows.  The last P.V is phase n_kv-1; phase
+    // n_kv-2 completed before S_i(n_kv-1) was published, so one phase behind.
+    if (ok && warp_wait(&bars->pv_done[wg], (n_kv - 1) & 1, 23, abort_flag)) {
       tc_fence_after();
       const int q_row = q0 + wg * BQ + row;
       const float inv_l = 1.0f / l_run;
@@ -328,8 +386,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(o_tmem + c * 32, r);
-        tc_wait_ld();
+        tmem_ld32p(o_tmem + c * 32, r);
+        tmem_wait_fence<1>(r);
         if (q_row < args.s_q) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -383,6 +441,7 @@ extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, vo
   CUtensorMap tq, tk, tv;
   int rc = h3b::encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, D, s_q, heads, q_seq_stride * 2,
                           q_head_stride * 2, 64, BQ, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  static_assert(BKV % 16 == 0 && BKV <= 256, "K/V tile rows");
   if (rc == H3B_OK)
     rc = h3b::encode_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, D, s_kv, heads, kv_seq_stride * 2,
                         kv_head_stride * 2, 64, BKV, 1, CU_TENSOR_MAP_SWIZZLE_128B);

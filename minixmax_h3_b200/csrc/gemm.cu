@@ -263,8 +263,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t t_row = tmem_base + buf * BN + (static_cast<uint32_t>(quad * 32) << 16);
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tc_wait_ld();
+        tmem_ld32p(t_row + c * 32, r);
+        tmem_wait_fence<1>(r);
         if (c == BN / 32 - 1) {
           tc_fence_before();
           mbar_arrive(&bars->acc_empty[buf]);

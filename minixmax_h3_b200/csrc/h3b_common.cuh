@@ -226,6 +226,30 @@ H3B_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// tcgen05.ld writes its registers asynchronously: they are valid only after
+// tcgen05.wait::ld.  The compiler does not know that, so after the wait the
+// registers are passed through an empty volatile asm that "modifies" them;
+// every later use then depends on a statement ordered after the wait.
+H3B_DEV void reg_fence32(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+// Load 32 columns into r[0..31] (pointer form of tmem_ld32).
+H3B_DEV void tmem_ld32p(uint32_t taddr, uint32_t* r) { tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r)); }
+
+// Wait for every outstanding tcgen05.ld of this thread and fence n*32 registers.
+template <int N>
+H3B_DEV void tmem_wait_fence(uint32_t* r) {
+  tc_wait_ld();
+#pragma unroll
+  for (int c = 0; c < N; ++c) reg_fence32(r + 32 * c);
+}
+
 H3B_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "

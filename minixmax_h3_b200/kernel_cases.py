@@ -1,0 +1,87 @@
+"""Single-kernel cases for profiling and timing sweeps.
+
+    python -m minixmax_h3_b200.kernel_cases attention --seq 131072 --heads 3
+    python -m minixmax_h3_b200.kernel_cases gemm_nvfp4 --m 8192 --n 9216 --k 3072
+    python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
+    python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases quant_i8 --m 32768 --k 3072
+
+Each case allocates its inputs once, launches the kernel `--warmup` times,
+then `--iters` times between CUDA events on the launching stream, and prints
+one JSON line (ms per launch and the algorithmic throughput).  Inputs are
+synthetic N(0,1) (weights N(0,0.02)).  Sizes are chosen by the caller so a
+profiler capture stays small.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import ops
+
+
+def _time(fn, warmup: int, iters: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / max(iters, 1)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8"])
+    ap.add_argument("--seq", type=int, default=16384)
+    ap.add_argument("--heads", type=int, default=24)
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=9216)
+    ap.add_argument("--k", type=int, default=3072)
+    ap.add_argument("--warmup", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=2)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    rec: dict = {"case": a.case}
+    if a.case == "attention":
+        q, k, v = (torch.randn(a.seq, a.heads, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        o = torch.empty_like(q)
+        ms = _time(lambda: ops.attention(q, k, v, out=o), a.warmup, a.iters)
+        flops = 4.0 * a.seq * a.seq * 128 * a.heads
+        rec.update(seq=a.seq, heads=a.heads, ms=ms, tflops=flops / ms / 1e9, flops=flops)
+    elif a.case in ("gemm_nvfp4", "gemm_i8"):
+        x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(a.n, a.k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        if a.case == "gemm_nvfp4":
+            xa, wq = ops.quant_nvfp4(x), ops.quant_nvfp4(w)
+            out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device=dev)
+            ms = _time(lambda: ops.gemm_nvfp4(xa, wq, out=out), a.warmup, a.iters)
+        else:
+            q, xs = ops.quant_i8_rows(x)
+            wq = torch.randint(-128, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g)
+            ws = torch.rand(a.n, device=dev, generator=g) * 1e-3
+            out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device=dev)
+            ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, out=out), a.warmup, a.iters)
+        flops = 2.0 * a.m * a.n * a.k
+        rec.update(m=a.m, n=a.n, k=a.k, ms=ms, tflops=flops / ms / 1e9, flops=flops)
+    else:
+        x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
+        if a.case == "quant_nvfp4":
+            amax = ops.amax(x)
+            ms = _time(lambda: ops.quant_nvfp4(x, amax_t=amax), a.warmup, a.iters)
+            nbytes = 2 * a.m * a.k + a.m * a.k // 2 + a.m * a.k // 16
+        else:
+            ms = _time(lambda: ops.quant_i8_rows(x), a.warmup, a.iters)
+            nbytes = 3 * a.m * a.k + 4 * a.m
+        rec.update(m=a.m, k=a.k, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
+    print(json.dumps(rec), flush=True)
+
+
+if __name__ == "__main__":
+    main()
