@@ -10,6 +10,7 @@
 //   warps 4-7   softmax for Q1
 //   warp 8      TMA producer: Q0/Q1 once, K and V through 2-deep rings
 //   warp 9      TMEM allocator + single-thread MMA issuer
+//   warps 10-11 idle (complete the third warpgroup for setmaxnreg)
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each.  The softmax
 // writes P as packed bf16 into the first 64 columns of the S region it read,
 // and P.V reads it straight from TMEM (tcgen05.mma with the A operand in
@@ -44,7 +45,13 @@ constexpr int Q_TILE_BYTES = BQ * D * 2;        // 32 KB: two 16 KB boxes (d 0-6
 constexpr int Q_HALF_BYTES = Q_TILE_BYTES / 2;
 constexpr int KV_TILE_BYTES = BKV * D * 2;      // 32 KB: two 16 KB boxes
 constexpr int KV_HALF_BYTES = KV_TILE_BYTES / 2;
-constexpr int THREADS = 320;
+constexpr int THREADS = 384;  // 3 warpgroups: softmax Q0, softmax Q1, load/MMA
+// Register split (setmaxnreg): launched at 168/thread (384 x 168 = 64512); the
+// load/MMA warpgroup drops to 56 and the two softmax warpgroups rise to 224:
+// 4*32*56 + 8*32*224 = 64512, exactly the launch allocation.
+constexpr int REGS_LOADER = 88;
+constexpr int REGS_SOFTMAX = 208;
+static_assert(4 * 32 * REGS_LOADER + 8 * 32 * REGS_SOFTMAX <= THREADS * 168, "register split exceeds launch");
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 constexpr uint32_t IDESC_S = idesc_bf16_f32(128, BKV, 0, 0);  // Q (K-major) x K^T (K-major)
@@ -61,7 +68,7 @@ struct __align__(8) Bars {
   uint64_t v_full[VST];
   uint64_t v_empty[VST];
   uint64_t s_full[2];      // [tile]: S_i(j) ready (tcgen05.commit)
-  uint64_t p_full[2];      // [tile]: P_i(j) written (128 softmax threads)
+  uint64_t p_half[2][2];   // [tile][half]: P_i(j) columns 64h..64h+63 written (one arrival per softmax warp)
   uint64_t pv_done[2];     // [tile]: O_i += P_i(j) V_j complete (tcgen05.commit)
   uint64_t drain;
   uint32_t tmem_base;
@@ -93,36 +100,88 @@ H3B_DEV float fast_exp2(float x) {
   return y;
 }
 
-// Row max of one 64-column S tile with 8 independent chains (MASK: columns
-// >= valid of the last K/V tile are padding).
+// Row max of one 64-column S tile: 8 independent chains of three-input max
+// (MASK: columns >= valid of the last K/V tile are padding).
 template <bool MASK>
 H3B_DEV float row_max64(const uint32_t* r, int valid) {
+  auto v = [&](int e) { return (!MASK || e < valid) ? __uint_as_float(r[e]) : -INFINITY; };
   float mx[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) mx[e] = (!MASK || e < valid) ? __uint_as_float(r[e]) : -INFINITY;
+  for (int c = 0; c < 8; ++c) mx[c] = fmax3(v(c), v(c + 8), v(c + 16));
 #pragma unroll
-  for (int e = 8; e < 64; ++e) mx[e & 7] = fmaxf(mx[e & 7], (!MASK || e < valid) ? __uint_as_float(r[e]) : -INFINITY);
-  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+  for (int e = 24; e < 64; e += 16) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) mx[c] = fmax3(mx[c], v(e + c), e + 8 + c < 64 ? v(e + 8 + c) : -INFINITY);
+  }
+  return fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
 }
 
-// p = exp2(s*scale_log2 - m) for 64 columns: summed in 4 chains, packed to
-// 32 bf16 pairs.
+// 2^x on the FMA pipe for a pair of lanes (FA4-style MUFU offload), from
+// Cody-Waite range reduction and a polynomial:
+//   x = n + f with n = round(x) (via the 1.5*2^23 magic add), f in [-1/2, 1/2]
+//   2^f ~= c0 + f(c1 + f(c2 + f c3)), a degree-3 fit of 2^f on [-1/2, 1/2]
+//        made for this kernel (relative-error weighted least squares on
+//        Chebyshev nodes, refined toward equi-ripple): max relative error
+//        7.5e-5, far below the 2^-9 rounding of the bf16 P it feeds
+//   2^x = 2^f * 2^n by adding n to the exponent field.
+// x is clamped to >= -125 so the exponent add cannot underflow (2^-125 is
+// zero for every downstream use); x <= 9 holds by the lazy-rescale bound.
+H3B_DEV float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992805719f, c1 = 0.69326102734f, c2 = 0.24261114001f, c3 = 0.05517161265f;
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = add2(x, make_float2(kMagic, kMagic));         // round(x) in the low mantissa bits
+  const float2 n = add2(t, make_float2(-kMagic, -kMagic));        // round(x) as a float (exact)
+  const float2 f = add2(x, make_float2(-n.x, -n.y));              // f in [-1/2, 1/2]
+  float2 p = fma2(make_float2(c3, c3), f, make_float2(c2, c2));
+  p = fma2(p, f, make_float2(c1, c1));
+  p = fma2(p, f, make_float2(c0, c0));
+  // t's bit pattern is 0x4B400000 + n; shifting it left by 23 leaves n << 23.
+  const uint32_t bx = __float_as_uint(p.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t by = __float_as_uint(p.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(bx), __uint_as_float(by));
+}
+
+// Pairs (out of every 8) whose exponentials go to the FMA pipe instead of MUFU.
+constexpr int POLY_PAIRS_PER_8 = 3;
+
+// In-place softmax numerator for 64 columns r[0..63] (fp32 S bits in, packed
+// bf16 P out in dst[0..31]): packed fp32x2 FMA, 64 independent exponentials
+// (split between MUFU ex2 and the FMA-pipe polynomial), then pack and packed
+// sums.  dst may alias r (dst[e] is written after r[2e], r[2e+1] are read,
+// and e <= 2e).  Returns the partial row sum.
 template <bool MASK>
-H3B_DEV float exp_pack64(const uint32_t* r, int valid, float scale_log2, float neg_m, uint32_t (&pk)[32]) {
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+H3B_DEV float exp_pack64(uint32_t* r, uint32_t* dst, int valid, float scale_log2, float neg_m) {
+  const float2 sc = make_float2(scale_log2, scale_log2);
+  const float2 nm = make_float2(neg_m, neg_m);
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const float sa = (!MASK || 2 * e < valid) ? __uint_as_float(r[2 * e]) : -INFINITY;
     const float sb = (!MASK || 2 * e + 1 < valid) ? __uint_as_float(r[2 * e + 1]) : -INFINITY;
-    const float a = fast_exp2(fmaf(sa, scale_log2, neg_m));
-    const float b = fast_exp2(fmaf(sb, scale_log2, neg_m));
-    acc[e & 3] += a + b;
-    pk[e] = pack_bf16x2(a, b);
+    float2 x = fma2(make_float2(sa, sb), sc, nm);
+    if ((e & 7) < POLY_PAIRS_PER_8) {
+      x = exp2_poly2(x);
+    } else {
+      x.x = fast_exp2(x.x);
+      x.y = fast_exp2(x.y);
+    }
+    r[2 * e] = __float_as_uint(x.x);
+    r[2 * e + 1] = __float_as_uint(x.y);
   }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const float2 p = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+    acc[e & 3] = add2(acc[e & 3], p);
+    dst[e] = pack_bf16x2(p.x, p.y);
+  }
+  const float2 t = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  return t.x + t.y;
 }
 
-// 10 warps: two SM sub-partitions host 3 warps, capping registers at 168.
+// 12 warps = 3 per SM sub-partition: launched at 168 registers per thread,
+// then rebalanced with setmaxnreg (see REGS_LOADER / REGS_SOFTMAX).
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
@@ -152,7 +211,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], 128);
+      mbar_init(&bars->p_half[i][0], 4);  // one arrival per softmax warp
+      mbar_init(&bars->p_half[i][1], 4);
       mbar_init(&bars->pv_done[i], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -168,6 +228,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  if (warp >= 8) {
+    // ------------------------------------------------------------ load / MMA warpgroup
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOADER));
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -240,18 +303,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&bars->s_full[i]);
       };
-      // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  p_full[i]
-      // completes once per tile; the softmax cannot arrive for j+1 before
-      // S_i(j+1), which is issued after this wait, so it is one phase behind.
+      // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  Each
+      // p_half[i][h] completes once per tile; the softmax cannot arrive for
+      // j+1 before S_i(j+1), which is issued after these waits, so each wait
+      // is one phase behind.
+      // P is published in two halves (K/V rows 0-63, 64-127) so the first
+      // half of P.V runs while the softmax computes the second.
       auto issue_pv = [&](int i, int j, uint32_t v_addr) -> bool {
-        if (!mbar_wait(&bars->p_full[i], j & 1, &g_status, 7, abort_flag)) return false;
-        tc_fence_after();
         const uint32_t p_tmem = tmem + s_col(i);
         const uint32_t o_tmem = tmem + o_col(i);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&bars->p_half[i][h], j & 1, &g_status, 7, abort_flag)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t bd = sdesc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF_BYTES, 1024);
-          mma_f16_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
+            const uint64_t bd = sdesc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF_BYTES, 1024);
+            mma_f16_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         tc_commit(&bars->pv_done[i]);
         return true;
@@ -289,8 +357,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
     }
+  }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
     const int wg = warp >> 2;                  // Q tile 0 / 1
     const int quad = warp & 3;
     const int row = quad * 32 + lane;          // row within the Q tile
@@ -309,18 +379,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_after();
       const int valid = args.s_kv - j * BKV;  // columns >= valid are padding
-      const bool full = valid >= BKV;
-      // Pass 1: row max over two 64-column halves.
-      float row_max = -INFINITY;
+      const bool full = valid >= BKV;  // uniform across the warp (same tile)
+      // One TMEM round trip: all 128 columns in flight, one wait.
+      uint32_t r[128];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r[64];
-        tmem_ld32p(s_tmem + h * 64, r);
-        tmem_ld32p(s_tmem + h * 64 + 32, r + 32);
-        tmem_wait_fence<2>(r);
-        const float m = full ? row_max64<false>(r, valid - h * 64) : row_max64<true>(r, valid - h * 64);
-        row_max = fmaxf(row_max, m);
+      for (int c = 0; c < 4; ++c) tmem_ld32p(s_tmem + c * 32, r + 32 * c);
+      tmem_wait_fence<4>(r);
+      if (!full) {  // last K/V tile only (warp-uniform): padding columns -> -inf
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (e >= valid) r[e] = __float_as_uint(-INFINITY);
       }
+      const float row_max = fmaxf(row_max64<false>(r, BKV), row_max64<false>(r + 64, BKV));
       const float m_tile = row_max * args.scale_log2;
       float m_use = m_run;
       bool rescale = false;
@@ -328,9 +398,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_use = m_tile;
         rescale = true;
       }
-      // The correction runs warp-uniformly: tcgen05.ld/st are .sync.aligned
-      // and warp_wait shuffles over the full warp, so a per-row branch here
-      // would deadlock the warp.  Rows that need no rescale use factor 1.
+      // O correction first: O must be rescaled before P_i(j).V starts.  It
+      // runs warp-uniformly: tcgen05.ld/st are .sync.aligned and warp_wait
+      // shuffles over the full warp, so a per-row branch here would deadlock
+      // the warp.  Rows that need no rescale use factor 1.
       if (__any_sync(0xffffffffu, rescale)) {
         const float factor = rescale ? fast_exp2(m_run - m_use) : 1.0f;  // 0 on the first tile
         l_run = l_run * factor;
@@ -355,24 +426,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (rescale) m_run = m_use;
       }
-      // Pass 2: P = exp2(s*scale - m) as packed bf16.  P half h covers columns
-      // 32h..32h+31, which overlap only S columns already loaded.
+      // P = exp2(s*scale - m) as packed bf16, published half by half: half h
+      // (K/V rows 64h..64h+63) lands in columns 32h..32h+31 over S columns
+      // already consumed.
       float sum = 0.0f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t r[64];
-        tmem_ld32p(s_tmem + h * 64, r);
-        tmem_ld32p(s_tmem + h * 64 + 32, r + 32);
-        tmem_wait_fence<2>(r);
-        uint32_t pk[32];
-        sum += full ? exp_pack64<false>(r, valid - h * 64, args.scale_log2, -m_use, pk)
-                    : exp_pack64<true>(r, valid - h * 64, args.scale_log2, -m_use, pk);
-        tmem_st32(s_tmem + h * 32, pk);
+        sum += exp_pack64<false>(r + 64 * h, r + 32 * h, BKV, args.scale_log2, -m_use);
+        tmem_st32(s_tmem + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * h));
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_half[wg][h]);
       }
       l_run += sum;
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars->p_full[wg]);
     }
     // ---- epilogue: O / l -> bf16 rows.  The last P.V is phase n_kv-1; phase
     // n_kv-2 completed before S_i(n_kv-1) was published, so one phase behind.

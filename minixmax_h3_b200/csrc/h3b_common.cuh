@@ -76,14 +76,16 @@ H3B_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// try_wait with an explicit suspend-time hint (ns): the thread sleeps until
+// the phase completes or the hint expires, whichever comes first.
 H3B_DEV bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred P;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, P;\n\t}"
       : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
+      : "r"(bar_addr), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
@@ -332,6 +334,30 @@ H3B_DEV float bf16hi_to_f32(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u
 H3B_DEV uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Packed fp32x2 arithmetic (sm_100): two lanes of work per instruction.
+H3B_DEV float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+H3B_DEV float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("add.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
+
+// Three-input max (sm_100): halves the instruction count of row maxima.
+H3B_DEV float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 H3B_DEV float warp_max(float v) {
