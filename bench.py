@@ -42,6 +42,7 @@ S_VIDEO = GRID[0] * GRID[1] * GRID[2]
 S_TOTAL = N_TEXT + S_VIDEO  # 498,272
 METRIC = "DiT-block tokens/s"
 REF_TOKENS, REF_Q_ROWS = 1024, 128  # CPU sample per reference step (~1 s of CPU work)
+ATTN_DRAM_BYTES_24_HEADS = 1.57e12 + 3.31e9  # ncu dram__bytes_read.sum + write.sum, one launch
 UNIT = "block-tokens/s"
 WORKLOAD = ("cfg5: one denoising step of 4 DiT blocks, hidden 3072, 24x128 heads, GELU MLP 12288, NVFP4 W4A4 "
             "linears, 512 text (dim 4096) + 497760 video tokens (t61 x h68 x w120) = 498272-token joint attention, "
@@ -289,11 +290,10 @@ def run_gpu(args) -> None:
     achieved = attn_flops / (attn_ms * 1e-3) / 1e12
     clock = clocks.summary()
     if rank == 0:
-        traffic = None
-        tf = ROOT / "profiles" / "attention_traffic.json"
-        if tf.exists():
-            d = json.loads(tf.read_text())
-            traffic = d.get("bytes_per_flop", 0.0) * attn_flops if d.get("bytes_per_flop") else None
+        # DRAM bytes of one full-size attention launch (S = 498,272, 24 heads),
+        # from the 1-pass ncu capture in profiles/attention_kernel_S131072_H3.md;
+        # a rank's launch covers HEADS/ws heads of the same sequence.
+        traffic = ATTN_DRAM_BYTES_24_HEADS * (HEADS // ws) / HEADS
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
             torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
