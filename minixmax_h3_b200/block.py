@@ -63,6 +63,18 @@ class RopeSpec:
         return torch.stack([tt.reshape(-1), hh.reshape(-1), ww.reshape(-1)], dim=-1).to(torch.float32)
 
 
+def global_amax_(amax: Optional[torch.Tensor], ql: QuantLinear) -> Optional[torch.Tensor]:
+    """Makes an NVFP4 activation's global scale independent of the GPU count:
+    under sequence parallelism each rank sees only its tokens, so the |x| max
+    feeding gs = amax/(6*448) is max-reduced across ranks (one float) before
+    the quantiser runs.  INT8 scales are per token and need nothing."""
+    if amax is not None and ql.quant_format == "nvfp4" and is_distributed():
+        import torch.distributed as tdist
+
+        tdist.all_reduce(amax, op=tdist.ReduceOp.MAX, group=state().group)
+    return amax
+
+
 def segments_to_row_sel(segments: Sequence[tuple[int, int, int]], s_len: int, device) -> torch.Tensor:
     """Per-token adaLN row index for (a, b, row) segments; -1 = no segment
     (such tokens are normalised but neither modulated nor gated, exactly as
@@ -145,7 +157,7 @@ class Attention(nn.Module):
         otherwise returns attn(h)."""
         s_local = h.shape[0]
         sp = self.sequence_parallel and is_distributed()
-        qkv = self.qkv_proj.forward_fused(h, amax=amax_h)  # [S_l, 3*H*D]
+        qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
         if rope_freqs is not None:
             s0 = split_range(rope_freqs.pos.shape[0])[0] if sp else 0
@@ -166,6 +178,7 @@ class Attention(nn.Module):
             o = all_to_all_heads(o, gather_seq=False).reshape(s_local, self.heads * self.head_dim)
             o = o.contiguous()
             ops.amax(o, out=amax_o)
+            global_amax_(amax_o, self.out_proj)
         else:
             flops = 4.0 * s_local * s_local * self.head_dim * self.heads
             o = ATTN_TIMER.record(lambda: ops.attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5,
@@ -195,12 +208,16 @@ class MLP(nn.Module):
 
     def forward(self, h: torch.Tensor, *, amax_h=None, resid=None, gate=None, row_sel=None) -> torch.Tensor:
         amax_u = torch.zeros(1, dtype=torch.float32, device=h.device)
+        amax_h = global_amax_(amax_h, self.fc1)
         if self.act == "gelu":
             u = self.fc1.forward_fused(h, amax=amax_h, epilogue=EPI_GELU, amax_out=amax_u)
+            global_amax_(amax_u, self.fc2)
         else:
             g, up = self.fc1.forward_fused(h, amax=amax_h).chunk(2, dim=-1)
             u = (F.silu(g) * up).contiguous()
             amax_u = None
+            if self.fc2.quant_format == "nvfp4" and is_distributed():
+                amax_u = global_amax_(ops.amax(u), self.fc2)
         if resid is not None:
             return self.fc2.forward_fused(u, amax=amax_u, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
                                           row_sel=row_sel)

@@ -1,0 +1,93 @@
+"""Multi-GPU parity of the Ulysses DiT block (needs >= 2 GPUs; skipped otherwise).
+
+Two NCCL ranks each run their sequence shard of one DiT block; the gathered
+result must match the same block run on one GPU.  With INT8 (per-token
+activation scales) every token sees identical arithmetic on both paths, so the
+match is exact.  With NVFP4 the activation global scales are max-reduced
+across ranks (block.global_amax_), so the sharded run quantises exactly as
+the single-GPU run and the match is exact too."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, ws: int, port: int, fmt: str, out_q) -> None:
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(ws),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as tdist
+
+    from minixmax_h3_b200 import dist as hdist
+    from minixmax_h3_b200.block import DiTBlock, RopeSpec, init_block_random
+    from minixmax_h3_b200.ulysses import clip_mod_segments, split_range
+
+    try:
+        st = hdist.init(timeout_s=120)
+        dev = torch.device("cuda", rank)
+        hidden, heads = 512, 4
+        blk = DiTBlock(hidden, heads, 128, 4 * hidden, 256, 1e-6, 1e-6, dtype=torch.bfloat16, device=dev,
+                       mlp_act="gelu")
+        init_block_random(blk, fmt, torch.Generator(device=dev).manual_seed(0))  # same on every rank
+        pos = RopeSpec.grid_positions(4, 16, 24)
+        rope = RopeSpec.build(pos, device=dev)
+        s_total = pos.shape[0]
+        x_full = torch.randn(s_total, hidden, generator=torch.Generator(device=dev).manual_seed(1),
+                             device=dev).to(torch.bfloat16)
+        t_emb = torch.randn(1, 256, generator=torch.Generator(device=dev).manual_seed(2), device=dev
+                            ).to(torch.bfloat16)
+        segs = [(0, 100, 1), (100, s_total - 16, 0)]
+        s0, s1 = split_range(s_total)
+        y_local = blk(x_full[s0:s1].clone(), t_emb, clip_mod_segments(segs, s0, s1), rope)
+        gathered = [torch.empty_like(y_local) for _ in range(ws)]
+        tdist.all_gather(gathered, y_local)
+        if rank == 0:
+            y_sp = torch.cat(gathered)
+            hdist.set_state(0, 1)  # single-GPU run of the same block on rank 0
+            y_one = blk(x_full.clone(), t_emb, segs, rope)
+            g, w = y_sp.float().cpu().reshape(-1), y_one.float().cpu().reshape(-1)
+            err = ((g - w).abs() / w.abs().clamp(min=1.0)).max().item()
+            cos = torch.nn.functional.cosine_similarity(g.double(), w.double(), dim=0).item()
+            out_q.put(("ok", torch.equal(y_sp.cpu(), y_one.cpu()), err, cos))
+            hdist.set_state(0, ws, group=tdist.group.WORLD, backend="nccl")
+        tdist.barrier(device_ids=[rank])
+        hdist.destroy()
+    except Exception as e:  # noqa: BLE001
+        out_q.put(("fail", repr(e), 0.0, 0.0))
+        raise
+
+
+@pytest.mark.parametrize("fmt", ["int8_tensorwise", "nvfp4"])
+def test_ulysses_block_matches_single_gpu(fmt):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, fmt, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        status, exact, err, cos = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert status == "ok", exact
+    assert exact, (err, cos)
