@@ -7,15 +7,25 @@
 //                  ue4m3 scale per 16 elements copied smem -> TMEM with
 //                  tcgen05.cp, epilogue y = acc * a_gs * w_gs (+ bias[n]).
 //
-// Structure (one CTA per SM, persistent over 128x256 output tiles):
-//   warp 0      TMA producer: A tile 128x128B, B tile 256x128B (+ scale
-//               factors by plain bulk copies) into a STAGES-deep smem ring.
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A tile 128x128B, B tile BNx128B (+ scale
+//               factors by plain bulk copies) into a 4-deep smem ring.
 //   warp 1      TMEM allocator and single-thread MMA issuer; tcgen05.commit
 //               releases smem slots and publishes finished accumulators.
 //   warps 2-5   epilogue: tcgen05.ld 32x32b (one output row per thread),
-//               fp32 dequant/bias/activation/gate-residual, bf16 stores.
-// Operands are K-major with the 128-byte swizzle on both the TMA and the UMMA
-// side.  Loads never use cluster multicast.  Every wait is bounded.
+//               fp32 dequant/bias/activation/gate-residual, bf16 rows staged
+//               in 64B-swizzled shared memory and written by TMA stores.
+// Accumulators are double-buffered in TMEM (columns 0 and 256), so the MMAs
+// of tile t+1 run while the epilogue drains tile t:
+//   INT8:  BN = 256.
+//   NVFP4: BN = 192, plus a 2-slot scale-factor ring at columns 192 and 448
+//          (48 columns per slot), refilled by tcgen05.cp in issue order
+//          behind the MMAs that read it.  A 192-row N tile starts either
+//          on a 128-row scale block (even tiles) or 64 rows into one (odd
+//          tiles): the two blocks covering it are copied and the MMA's SFB
+//          address skips 2 TMEM columns (= 64 rows) for odd tiles.
+// Operands are K-major with the 128-byte swizzle.  No load uses cluster
+// multicast.  Every wait is bounded.
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
 
@@ -25,14 +35,14 @@ H3B_REGISTER_STATUS_READER(gemm);
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
-constexpr int B_BYTES = BN * 128;
 constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
-constexpr int SFB_BYTES = 4096;    // 256 rows x 16 scales
+constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
 constexpr int EPI_THREADS = 128;
 constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 staging buffer
+constexpr int ACC_STRIDE = 256;           // TMEM columns between the two accumulators
 
 enum Kind { KIND_I8 = 0, KIND_NVF4 = 1 };
 enum OutMode { OUT_BF16 = 0, OUT_I32 = 1 };
@@ -59,14 +69,21 @@ struct GemmArgs {
 
 template <int KIND>
 struct Cfg {
-  static constexpr int NACC = KIND == KIND_I8 ? 2 : 1;          // accumulator buffers
-  static constexpr int SF_COL0 = NACC * BN;                      // TMEM column of the SF ring
-  static constexpr int SF_COLS_PER_STAGE = 48;                   // 16 (A) + 32 (B)
+  static constexpr int BN = KIND == KIND_I8 ? 256 : 192;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int SF_COLS_PER_SLOT = 48;  // 16 (A) + 32 (B)
   static constexpr int TMEM_COLS = 512;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + (KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0);
+  static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
   static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
   static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM, BN) : idesc_nvf4(BM, BN);
+  static_assert(BN <= ACC_STRIDE, "accumulator overlap");
+  static_assert(KIND == KIND_I8 || BN + SF_COLS_PER_SLOT <= ACC_STRIDE, "SF slot overlaps an accumulator");
+  static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 };
+
+// TMEM column of scale-factor slot `slot` (NVFP4): just past each accumulator.
+H3B_DEV uint32_t sf_slot_col(int slot) { return 192u + static_cast<uint32_t>(slot) * ACC_STRIDE; }
 
 struct __align__(8) Barriers {
   uint64_t full[STAGES];
@@ -81,7 +98,8 @@ struct __align__(8) Barriers {
 
 template <int KIND>
 constexpr size_t smem_bytes() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * Cfg<KIND>::STAGE_BYTES + sizeof(Barriers);
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * Cfg<KIND>::STAGE_BYTES +
+         4 * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
 }
 
 H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
@@ -93,23 +111,30 @@ H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* a
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Byte offset of 16-byte chunk c of row r in a 32-row x 64-byte staging
+// buffer in the TMA 64-byte swizzle (address bits 4-5 ^= bits 7-8).  The
+// buffer must be 512-byte aligned.
+H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
+
 template <int KIND>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmap_y, const GemmArgs args) {
   using C = Cfg<KIND>;
+  constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sSFA = sB + STAGES * B_BYTES;                 // used by KIND_NVF4 only
+  uint8_t* sSFA = sB + STAGES * C::B_BYTES;             // used by KIND_NVF4 only
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;       // 4 warps x 2 staging buffers, 1024-aligned
+  Barriers* bars = reinterpret_cast<Barriers*>(sOut + 4 * 2 * OUT_STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int m_tiles = (args.m + BM - 1) / BM;
-  const int n_tiles = args.n / BN + ((args.n % BN) ? 1 : 0);
+  const int n_tiles = (args.n + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int nk = args.k / C::K_PER_STAGE;
   volatile int* abort_flag = &bars->abort_flag;
@@ -129,6 +154,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_y);
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -145,8 +171,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * BM;
-        const int n0 = (tile % n_tiles) * BN;
+        const int mt = tile / n_tiles, nt = tile % n_tiles;
+        const int m0 = mt * BM;
+        const int n0 = nt * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const int round = it / STAGES;
@@ -156,14 +183,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
           tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * 128, m0, &bars->full[s]);
-          tma_load_2d(sB + s * B_BYTES, &tmap_b, kb * 128, n0, &bars->full[s]);
+          tma_load_2d(sB + s * C::B_BYTES, &tmap_b, kb * 128, n0, &bars->full[s]);
           if constexpr (KIND == KIND_NVF4) {
             const int64_t ncb = args.k / 64;  // 64-element scale groups per row
-            const uint8_t* sfa = args.a_sf + ((static_cast<int64_t>(m0 / 128) * ncb) + kb * 4) * 512;
-            const uint8_t* sfb0 = args.w_sf + ((static_cast<int64_t>(n0 / 128) * ncb) + kb * 4) * 512;
-            // A 128-column tail tile has no second scale block: reload the
-            // first one (in bounds); those output columns are never stored.
-            const int nb1 = (n0 + 128 < args.n) ? n0 / 128 + 1 : n0 / 128;
+            const uint8_t* sfa = args.a_sf + ((static_cast<int64_t>(mt) * ncb) + kb * 4) * 512;
+            // The 128-row scale blocks that cover rows n0 .. n0+191.  Past the
+            // last block the first is reloaded (in bounds; those output
+            // columns are never stored).
+            const int nb0 = n0 / 128;
+            const int nb1 = (nb0 + 1) * 128 < args.n ? nb0 + 1 : nb0;
+            const uint8_t* sfb0 = args.w_sf + ((static_cast<int64_t>(nb0) * ncb) + kb * 4) * 512;
             const uint8_t* sfb1 = args.w_sf + ((static_cast<int64_t>(nb1) * ncb) + kb * 4) * 512;
             bulk_load(sSFA + s * SFA_BYTES, sfa, SFA_BYTES, &bars->full[s]);
             bulk_load(sSFB + s * SFB_BYTES, sfb0, SFB_BYTES / 2, &bars->full[s]);
@@ -187,14 +216,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       int local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        const int buf = local % C::NACC;
-        const int use = local / C::NACC;
+        const int buf = local & 1;
+        const int use = local >> 1;
         if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * ACC_STRIDE;
+        // Odd 192-wide N tiles start 64 rows into their first scale block.
+        const uint32_t sfb_skip = (KIND == KIND_NVF4 && ((tile % n_tiles) & 1)) ? 2u : 0u;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&bars->full[s], (it / STAGES) & 1, &g_status, 3, abort_flag)) {
@@ -204,14 +235,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           *reinterpret_cast<volatile int*>(&bars->consumed) = it + 1;
           tc_fence_after();
           const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(sA + s * A_BYTES));
-          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(sB + s * B_BYTES));
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(sB + s * C::B_BYTES));
           if constexpr (KIND == KIND_I8) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
             }
           } else {
-            const uint32_t sf_col = tmem_base + C::SF_COL0 + s * C::SF_COLS_PER_STAGE;
+            // tcgen05.cp and tcgen05.mma issued by this one thread execute in
+            // issue order in the tensor pipe, so refilling slot it&1 cannot
+            // overtake the MMAs of slab it-2 that read it (the pattern
+            // CUTLASS's block-scaled mainloop relies on with a single slot).
+            const uint32_t sf_col = tmem_base + sf_slot_col(it & 1);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               tc_cp_32x128b_x4(sf_col + j * 4, sdesc_plain_rows16(smem_u32(sSFA + s * SFA_BYTES + j * 512)));
@@ -222,8 +257,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4, sf_col + 16 + j * 8,
-                          (kb | j) != 0);
+              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
+                          sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
             }
           }
           tc_commit(&bars->empty[s]);  // slot reusable once these MMAs have read it
@@ -239,11 +274,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    uint8_t* out_stage = sOut + quad * 2 * OUT_STAGE_BYTES;
     float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
+    int stage_seq = 0;                      // alternates this warp's two staging buffers
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int buf = local % C::NACC;
-      const int use = local / C::NACC;
+      const int buf = local & 1;
+      const int use = local >> 1;
       if (!warp_wait(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
       tc_fence_after();
       const int m0 = (tile / n_tiles) * BM;
@@ -260,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         row_scale = (*args.a_gs) * (*args.w_gs);
       }
-      const uint32_t t_row = tmem_base + buf * BN + (static_cast<uint32_t>(quad * 32) << 16);
+      const uint32_t t_row = tmem_base + buf * ACC_STRIDE + (static_cast<uint32_t>(quad * 32) << 16);
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32p(t_row + c * 32, r);
@@ -270,12 +307,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive(&bars->acc_empty[buf]);
         }
         const int col0 = n0 + c * 32;
-        if (!row_ok || col0 >= args.n) continue;
+        if (col0 >= args.n) continue;  // warp-uniform: the whole chunk is past the last column
         if (args.out_mode == OUT_I32) {
-          int32_t* out = static_cast<int32_t*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
+          if (row_ok) {
+            int32_t* out = static_cast<int32_t*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            *reinterpret_cast<uint4*>(out + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+            for (int j = 0; j < 32; j += 4) {
+              *reinterpret_cast<uint4*>(out + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+            }
           }
           continue;
         }
@@ -294,11 +333,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (args.bias != nullptr) a = __fadd_rn(a, __bfloat162float(args.bias[col0 + j]));
           v[j] = a;
         }
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
         if (args.epilogue == H3B_EPI_GELU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-        } else if (args.epilogue == H3B_EPI_GATE_RES) {
+        } else if (args.epilogue == H3B_EPI_GATE_RES && row_ok) {
           const __nv_bfloat16* res = args.resid + static_cast<int64_t>(row) * args.ldy + col0;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -313,20 +351,36 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+        // Stage the 32x32 bf16 block and TMA-store it.  A staging buffer is
+        // reused every other block: first wait until at most one store (the
+        // other buffer's) may still be reading shared memory.
+        uint8_t* sb = out_stage + (stage_seq & 1) * OUT_STAGE_BYTES;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int j = q4 * 8;
           const uint4 pk = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
                                       pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
-          *reinterpret_cast<uint4*>(out + j) = pk;
-          if (args.amax_out != nullptr) {
+          *reinterpret_cast<uint4*>(sb + swz64(lane, q4)) = pk;
+          if (args.amax_out != nullptr && row_ok) {
             const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
           }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_y, sb, col0, m0 + quad * 32);  // rows >= m are clipped by the map
+          bulk_commit_group();
+        }
+        ++stage_seq;
       }
     }
+    if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
+    __syncwarp();
     if (args.amax_out != nullptr) {
       y_amax = warp_max(y_amax);
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(args.amax_out), __float_as_uint(y_amax));
@@ -344,13 +398,22 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int KIND>
 int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                 cudaStream_t st) {
-  CUtensorMap ta, tb;
+  using C = Cfg<KIND>;
+  CUtensorMap ta, tb, ty;
   int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
-  rc = h3b::encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, b_row_bytes, args.n, b_row_bytes, 128, BN,
+  rc = h3b::encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, b_row_bytes, args.n, b_row_bytes, 128, C::BN,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
+  if (args.out_mode == OUT_BF16) {
+    // y viewed as [m rows, n cols] bf16 with row pitch ldy; 32x32 boxes.
+    rc = h3b::encode_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, args.y, args.n, args.m, args.ldy * 2, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != H3B_OK) return rc;
+  } else {
+    ty = ta;  // the int32 path stores directly; the map is never used
+  }
   const size_t smem = smem_bytes<KIND>();
   static bool attr_set[2] = {false, false};
   if (!attr_set[KIND]) {
@@ -360,10 +423,10 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
     attr_set[KIND] = true;
   }
   const int m_tiles = static_cast<int>((args.m + BM - 1) / BM);
-  const int n_tiles = static_cast<int>((args.n + BN - 1) / BN);
+  const int n_tiles = static_cast<int>((args.n + C::BN - 1) / C::BN);
   const int tiles = m_tiles * n_tiles;
   const int grid = tiles < h3b::num_sms() ? tiles : h3b::num_sms();
-  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, args);
+  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, ty, args);
   return h3b::launch_status();
 }
 
@@ -434,7 +497,6 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
     return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 256);
   if (rc != H3B_OK) return rc;
-  if ((n % 128) != 0) return H3B_ERR_SHAPE;  // whole 128-row scale blocks for B
   if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;

@@ -94,7 +94,12 @@ def _nvfp4_operands(cuda, m, n, k, seed):
     return x, w, a, wq
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (300, 384, 512), (1000, 3072, 3072), (200, 256, 12288)])
+# n = 160 and 448 end in a partial 192-wide tile; 384 and 3072 exercise the odd
+# tiles whose weight scales start 64 rows into a 128-row block.
+@pytest.mark.parametrize(
+    "m,n,k",
+    [(128, 256, 256), (300, 384, 512), (1000, 3072, 3072), (200, 256, 12288), (64, 160, 512), (130, 448, 256)],
+)
 def test_nvfp4_gemm(cuda, m, n, k):
     from minixmax_h3_b200 import ops
 
