@@ -81,6 +81,21 @@ H3B_API int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t k, 
                       float* scale, h3b_stream_t stream);
 
 /*
+ * ConvRot variant of h3b_quant_i8_rows: each 256-column group of a row is
+ * first multiplied by the regular Hadamard matrix H4 (x) H4 (x) H4 (x) H4 / 16
+ * (H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]]), rounded once to the
+ * input dtype, then quantised as above.  Replaces ops/int8_convrot.py:139-157
+ * (rotate_activation of ops/hadamard.py:35-44 followed by
+ * _dynamic_quant_rows) for QuantLinear weights with meta "convrot".
+ * group_size must be 256 (the reference's default convrot_groupsize,
+ * modules/linear.py:149-151); k % 256 == 0, k <= 12288.  x_rot, if not NULL,
+ * receives the rotated activation [m, k] dense in the input dtype.
+ */
+H3B_API int h3b_quant_i8_rows_convrot(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx,
+                                      int64_t group_size, int8_t* q, float* scale, void* x_rot,
+                                      h3b_stream_t stream);
+
+/*
  * W8A8 GEMM on tcgen05 kind::i8 with int32 accumulation in TMEM:
  * y[m,n] = epi(acc[m,n] * xs[m] * ws[n] + bias[n]) as bf16, acc = sum_k
  * q[m,k]*w[n,k].  Replaces ops/int8_convrot.py:75-96 (torch_npu.

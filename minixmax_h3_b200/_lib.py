@@ -20,6 +20,7 @@ SIGNATURES: dict[str, list] = {
     "h3b_version": [],
     "h3b_device_status": [c_ptr, c_int],
     "h3b_quant_i8_rows": [c_ptr, c_int, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr],
+    "h3b_quant_i8_rows_convrot": [c_ptr, c_int, c_i64, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr],
     "h3b_gemm_i8_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_int,
                          c_i64, c_i64, c_i64, c_ptr],
     "h3b_gemm_i8_acc_i32": [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr],

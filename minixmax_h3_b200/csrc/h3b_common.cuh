@@ -266,6 +266,13 @@ H3B_DEV void reg_fence32(uint32_t* r) {
 // Load 32 columns into r[0..31] (pointer form of tmem_ld32).
 H3B_DEV void tmem_ld32p(uint32_t taddr, uint32_t* r) { tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r)); }
 
+H3B_DEV void reg_fence16(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
 // Wait for every outstanding tcgen05.ld of this thread and fence n*32 registers.
 template <int N>
 H3B_DEV void tmem_wait_fence(uint32_t* r) {

@@ -104,6 +104,158 @@ __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restr
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// ---------------------------------------------------------------- ConvRot
+// Online activation rotation of ops/hadamard.py:35-44 (rotate_activation):
+// every 256-column group of a row is multiplied by the regular Hadamard
+// matrix H = H4 (x) H4 (x) H4 (x) H4 / 16, H4 = [[1,1,1,-1],[1,1,-1,1],
+// [1,-1,1,1],[-1,1,1,1]] (hadamard.py:11-32), then the row is quantised as
+// in quant_i8_rows_kernel (int8_convrot.py:139-157 rotates, then calls
+// _dynamic_quant_rows).
+//
+// The product is computed exactly and rounded once: inputs are 16-bit
+// floats, coefficients +-1, so every partial sum of a group is exact in fp64
+// unless the group's magnitudes span more than 2^37; the result is scaled by
+// 1/16 (exact) and converted with one round-to-nearest-even to the input
+// type.  (The reference's value comes from a 16-bit GEMM whose fp32
+// accumulation order belongs to its backend.)  H is symmetric, so x.H = H.x,
+// and H applies H4 along each base-4 digit of the column index in turn.
+
+template <typename T>
+H3B_DEV T f64_round(double v);
+template <>
+H3B_DEV __nv_bfloat16 f64_round<__nv_bfloat16>(double v) {
+  unsigned short h;
+  asm("cvt.rn.bf16.f64 %0, %1;" : "=h"(h) : "d"(v));
+  return __ushort_as_bfloat16(h);
+}
+template <>
+H3B_DEV __half f64_round<__half>(double v) {
+  unsigned short h;
+  asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(v));
+  return __ushort_as_half(h);
+}
+
+// H4 along one base-4 digit whose two index bits are lane bits (lo, hi):
+// y = (sum of the 4 values) - 2 * (value at both bits flipped).
+template <int LO, int HI>
+H3B_DEV void h4_lanes(double (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    double s = v[e] + __shfl_xor_sync(0xffffffffu, v[e], LO);
+    s += __shfl_xor_sync(0xffffffffu, s, HI);
+    const double p = __shfl_xor_sync(0xffffffffu, v[e], LO | HI);
+    v[e] = s - 2.0 * p;
+  }
+}
+
+// x.H (unscaled) for the 256-element group held by one warp: lane l holds
+// columns 8l .. 8l+7.  Column index bits 0-2 are the element, 3-7 the lane;
+// the digits are bits (0,1), (2,3), (4,5), (6,7).
+H3B_DEV void hadamard256_warp(double (&v)[8]) {
+#pragma unroll
+  for (int b = 0; b < 8; b += 4) {  // digit bits 0,1: within the thread
+    const double s = (v[b] + v[b + 1]) + (v[b + 2] + v[b + 3]);
+    const double y0 = s - 2.0 * v[b + 3], y1 = s - 2.0 * v[b + 2];
+    const double y2 = s - 2.0 * v[b + 1], y3 = s - 2.0 * v[b];
+    v[b] = y0;
+    v[b + 1] = y1;
+    v[b + 2] = y2;
+    v[b + 3] = y3;
+  }
+  {  // digit bits 2,3: element bit 2 and lane bit 0
+    double t[4], w[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      t[e] = v[e] + v[e + 4];
+      t[e] += __shfl_xor_sync(0xffffffffu, t[e], 1);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = t[e & 3] - 2.0 * __shfl_xor_sync(0xffffffffu, v[e ^ 4], 1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = w[e];
+  }
+  h4_lanes<2, 4>(v);    // digit bits 4,5 = lane bits 1,2
+  h4_lanes<8, 16>(v);   // digit bits 6,7 = lane bits 3,4
+}
+
+// One CTA (8 warps) per row; warp w rotates groups w, w+8, ... (at most
+// MAXG each), keeps the rounded values, then the row is quantised.
+template <typename T, int MAXG>
+__global__ void __launch_bounds__(256) quant_i8_rows_rot_kernel(const T* __restrict__ x, int64_t k, int64_t ldx,
+                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                 T* __restrict__ x_rot) {
+  __shared__ float red[33];
+  const int64_t row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = static_cast<int>(k >> 8);
+  const T* xr = x + row * ldx;
+  float f[MAXG][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXG; ++i) {
+    const int g = warp + 8 * i;
+    if (g < groups) {  // warp-uniform
+      const uint4 raw = ld_nc_v4(xr + static_cast<int64_t>(g) * 256 + lane * 8);
+      float in[8];
+      unpack8<T>(raw, in);
+      double v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = static_cast<double>(in[e]);
+      hadamard256_warp(v);
+      uint32_t packed[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const T a = f64_round<T>(v[e] * 0.0625), b = f64_round<T>(v[e + 1] * 0.0625);
+        f[i][e] = static_cast<float>(a);
+        f[i][e + 1] = static_cast<float>(b);
+        packed[e >> 1] = static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&a)) |
+                         (static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&b)) << 16);
+        amax = fmaxf(amax, fmaxf(fabsf(f[i][e]), fabsf(f[i][e + 1])));
+      }
+      if (x_rot != nullptr)
+        *reinterpret_cast<uint4*>(x_rot + row * k + static_cast<int64_t>(g) * 256 + lane * 8) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  }
+  amax = block_max<256>(amax, red);
+  amax = fmaxf(amax, 1e-12f);
+  const float s = __fdiv_rn(amax, 127.0f);
+  int8_t* qr = q + row * k;
+#pragma unroll
+  for (int i = 0; i < MAXG; ++i) {
+    const int g = warp + 8 * i;
+    if (g < groups) {
+      uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float r = rintf(__fdiv_rn(f[i][j], s));
+        r = fminf(fmaxf(r, -128.0f), 127.0f);
+        const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
+        packed[j >> 2] |= b << ((j & 3) * 8);
+      }
+      *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(g) * 256 + lane * 8) = make_uint2(packed[0], packed[1]);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <typename T>
+int launch_quant_i8_rot(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q, float* scale, void* x_rot,
+                        cudaStream_t st) {
+  const T* xt = static_cast<const T*>(x);
+  T* xr = static_cast<T*>(x_rot);
+  const int64_t groups = k / 256;
+  const unsigned grid = static_cast<unsigned>(m);
+  if (groups <= 16) {
+    quant_i8_rows_rot_kernel<T, 2><<<grid, 256, 0, st>>>(xt, k, ldx, q, scale, xr);
+  } else if (groups <= 48) {
+    quant_i8_rows_rot_kernel<T, 6><<<grid, 256, 0, st>>>(xt, k, ldx, q, scale, xr);
+  } else {
+    return H3B_ERR_SHAPE;
+  }
+  return h3b::launch_status();
+}
+
 __global__ void __launch_bounds__(256) amax_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t nvec,
                                                         float* __restrict__ out) {
   __shared__ float red[33];
@@ -249,6 +401,21 @@ extern "C" int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (x_dtype == H3B_BF16) return launch_quant_i8<__nv_bfloat16>(x, m, k, ldx, q, scale, st);
   if (x_dtype == H3B_F16) return launch_quant_i8<__half>(x, m, k, ldx, q, scale, st);
+  return H3B_ERR_DTYPE;
+}
+
+extern "C" int h3b_quant_i8_rows_convrot(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx,
+                                         int64_t group_size, int8_t* q, float* scale, void* x_rot,
+                                         h3b_stream_t stream) {
+  if (x == nullptr || q == nullptr || scale == nullptr) return H3B_ERR_ARG;
+  if (group_size != 256) return H3B_ERR_SHAPE;
+  if (m < 0 || k <= 0 || (k % 256) != 0 || ldx < k || (ldx % 8) != 0 || m > 0x7fffffff) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) != 0) return H3B_ERR_ALIGN;
+  if (x_rot != nullptr && !h3b::aligned16(x_rot)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (x_dtype == H3B_BF16) return launch_quant_i8_rot<__nv_bfloat16>(x, m, k, ldx, q, scale, x_rot, st);
+  if (x_dtype == H3B_F16) return launch_quant_i8_rot<__half>(x, m, k, ldx, q, scale, x_rot, st);
   return H3B_ERR_DTYPE;
 }
 

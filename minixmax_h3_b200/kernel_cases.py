@@ -5,6 +5,7 @@
     python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8 --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases quant_i8_convrot --m 32768 --k 3072
 
 Each case allocates its inputs once, launches the kernel `--warmup` times,
 then `--iters` times between CUDA events on the launching stream, and prints
@@ -37,7 +38,8 @@ def _time(fn, warmup: int, iters: int) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8"])
+    ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8",
+                                       "quant_i8_convrot"])
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--heads", type=int, default=24)
     ap.add_argument("--m", type=int, default=8192)
@@ -77,7 +79,8 @@ def main() -> None:
             ms = _time(lambda: ops.quant_nvfp4(x, amax_t=amax), a.warmup, a.iters)
             nbytes = 2 * a.m * a.k + a.m * a.k // 2 + a.m * a.k // 16
         else:
-            ms = _time(lambda: ops.quant_i8_rows(x), a.warmup, a.iters)
+            group = 256 if a.case == "quant_i8_convrot" else 0
+            ms = _time(lambda: ops.quant_i8_rows(x, convrot_group=group), a.warmup, a.iters)
             nbytes = 3 * a.m * a.k + 4 * a.m
         rec.update(m=a.m, k=a.k, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
     print(json.dumps(rec), flush=True)

@@ -114,8 +114,10 @@ class QuantLinear(nn.Module):
         self.quant_format = meta.get("format")
         self.convrot = bool(meta.get("convrot", False))
         self.group_size = int(meta.get("convrot_groupsize", 256))
-        if self.convrot:
-            raise NotImplementedError("ConvRot (online Hadamard) checkpoints are not supported by this build")
+        # ConvRot only changes the INT8 path (ops/int8_convrot.py:139-140);
+        # the NVFP4 path ignores the flag, as the reference's does.
+        if self.convrot and self.quant_format == "int8_tensorwise" and self.group_size != 256:
+            raise NotImplementedError(f"ConvRot group size {self.group_size}: this build rotates 256-column groups")
         self.weight = nn.Parameter(torch.empty(0, device=device), requires_grad=False)
         if self.quant_format == "int8_tensorwise":
             self.weight_i8 = weight.to(device=device, dtype=torch.int8).contiguous()
@@ -168,7 +170,7 @@ class QuantLinear(nn.Module):
         amax: precomputed max|x| (fp32 device scalar) for the NVFP4 global
         scale, e.g. from the producing kernel; computed here when None."""
         if self.quant_format == "int8_tensorwise":
-            q, xs = ops.quant_i8_rows(x)
+            q, xs = ops.quant_i8_rows(x, convrot_group=self.group_size if self.convrot else 0)
             return ops.gemm_i8(q, xs, self.weight_i8, self.weight_scale, self._bias(x), epilogue=epilogue,
                                resid=resid, gate=gate, row_sel=row_sel, amax_out=amax_out, out=out)
         if self.quant_format == "nvfp4":

@@ -42,16 +42,28 @@ def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
 # ----------------------------------------------------------------------------- INT8
 
 
-def quant_i8_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per-row dynamic INT8 quantisation -> (q int8 [m,k], scale fp32 [m])."""
-    _cuda(x)
+def quant_i8_rows(x: torch.Tensor, *, convrot_group: int = 0,
+                  x_rot_out: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row dynamic INT8 quantisation -> (q int8 [m,k], scale fp32 [m]).
+
+    convrot_group=256 first rotates every 256-column group by the regular
+    Hadamard matrix (ConvRot, ops/hadamard.py:35-44); x_rot_out, if given
+    (dense [m, k], x's dtype), receives the rotated activation."""
+    _cuda(x, x_rot_out)
     if x.dtype not in (torch.bfloat16, torch.float16):
         raise TypeError("quant_i8_rows expects bf16/fp16 input")
     x2, m, k, ld = _rows(x)
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m,), dtype=torch.float32, device=x.device)
-    call("h3b_quant_i8_rows", x2.data_ptr(), 0 if x.dtype == torch.bfloat16 else 1, m, k, ld, q.data_ptr(),
-         s.data_ptr(), _stream(x))
+    dt = 0 if x.dtype == torch.bfloat16 else 1
+    if convrot_group:
+        if x_rot_out is not None and (x_rot_out.shape != (m, k) or x_rot_out.dtype != x.dtype
+                                      or not x_rot_out.is_contiguous()):
+            raise ValueError("x_rot_out must be a dense [m, k] tensor of x's dtype")
+        call("h3b_quant_i8_rows_convrot", x2.data_ptr(), dt, m, k, ld, int(convrot_group), q.data_ptr(),
+             s.data_ptr(), x_rot_out.data_ptr() if x_rot_out is not None else None, _stream(x))
+    else:
+        call("h3b_quant_i8_rows", x2.data_ptr(), dt, m, k, ld, q.data_ptr(), s.data_ptr(), _stream(x))
     return q, s
 
 

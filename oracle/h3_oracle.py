@@ -43,6 +43,54 @@ def dynamic_quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, scale
 
 
+H4 = ((1, 1, 1, -1), (1, 1, -1, 1), (1, -1, 1, 1), (-1, 1, 1, 1))
+
+
+def hadamard_matrix(size: int) -> np.ndarray:
+    """Regular Hadamard H4 (x) ... (x) H4 / sqrt(size) in fp64
+    (ops/hadamard.py:11-32: kron powers of the H4 seed, size a power of 4)."""
+    if size < 4 or size & (size - 1) or (size.bit_length() - 1) % 2:
+        raise ValueError("size must be a power of 4")
+    h4 = np.array(H4, dtype=np.float64)
+    h = h4
+    while h.shape[0] < size:
+        h = np.kron(h, h4)
+    return h / np.sqrt(size)
+
+
+def round_f64_to_16(v: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
+    """One round-to-nearest-even from fp64 to bf16 / fp16 (no intermediate
+    fp32 rounding).  bf16: the fp64 significand is rounded at bit 45 (keeping
+    8 significant bits), exact for results in the bf16 normal range; fp16:
+    numpy's direct double->half conversion."""
+    v = np.ascontiguousarray(v, dtype=np.float64)
+    if dtype == torch.float16:
+        return torch.from_numpy(v.astype(np.float16))
+    if dtype != torch.bfloat16:
+        raise TypeError(dtype)
+    u = v.view(np.uint64)
+    keep = (u >> np.uint64(45)) & np.uint64(1)
+    r = (u + np.uint64((1 << 44) - 1) + keep) & ~np.uint64((1 << 45) - 1)
+    f32 = r.view(np.float64).astype(np.float32)  # exact: 8 significant bits
+    return torch.from_numpy(f32).to(torch.bfloat16)  # exact truncation
+
+
+def rotate_activation_exact(x: torch.Tensor, group_size: int = 256) -> torch.Tensor:
+    """ConvRot online rotation (ops/hadamard.py:35-44): every group of
+    `group_size` columns times the regular Hadamard matrix, in x's 16-bit
+    dtype.  Restated as the exact product (fp64 holds every partial sum of
+    16-bit inputs with +-1 coefficients exactly for groups whose magnitudes
+    span under 2^37) rounded once to the output dtype; the reference's value
+    comes from a 16-bit GEMM with backend-defined fp32 accumulation order."""
+    *lead, k = x.shape
+    if k % group_size:
+        raise ValueError("k must be a multiple of group_size")
+    h = hadamard_matrix(group_size)
+    xd = x.reshape(-1, group_size).to(torch.float64).numpy()
+    y = xd @ h
+    return round_f64_to_16(y, x.dtype).reshape(*lead, k)
+
+
 def quantize_weight_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Symmetric per-output-channel INT8 weights (harness; the reference ships
     pre-quantised checkpoints, load/safetensors_quant.py:65-78)."""
@@ -340,9 +388,11 @@ class EmulatedQuantLinear(torch.nn.Module):
     """Quantised linear evaluated on the CPU: the operand quantisation of the
     CUDA path, dequantised exactly, product in fp64, output bf16."""
 
-    def __init__(self, weight: torch.Tensor, fmt: str, bias: Optional[torch.Tensor] = None):
+    def __init__(self, weight: torch.Tensor, fmt: str, bias: Optional[torch.Tensor] = None,
+                 convrot: bool = False):
         super().__init__()
         self.fmt = fmt
+        self.convrot = convrot
         self.bias = bias
         self.out_features, self.in_features = weight.shape
         if fmt == "int8":
@@ -356,6 +406,8 @@ class EmulatedQuantLinear(torch.nn.Module):
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16)
         if self.fmt == "int8":
+            if self.convrot:  # ops/int8_convrot.py:139-140: rotate, then quantise
+                x2 = rotate_activation_exact(x2, 256)
             q, xs = dynamic_quant_rows(x2)
             y = w8a8_linear(q, xs, self.wq, self.ws, self.bias)
         else:

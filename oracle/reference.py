@@ -24,8 +24,8 @@ def load() -> Optional[SimpleNamespace]:
         sys.path.insert(0, REF_SRC)
     from h3_npu.model import dit
     from h3_npu.modules import linear
-    from h3_npu.ops import attention, float8_cast, int8_convrot, nvfp4, rope, ulysses
+    from h3_npu.ops import attention, float8_cast, hadamard, int8_convrot, nvfp4, rope, ulysses
     from h3_npu.runtime import dist
 
     return SimpleNamespace(dit=dit, linear=linear, attention=attention, float8_cast=float8_cast,
-                           int8_convrot=int8_convrot, nvfp4=nvfp4, rope=rope, ulysses=ulysses, dist=dist)
+                           hadamard=hadamard, int8_convrot=int8_convrot, nvfp4=nvfp4, rope=rope, ulysses=ulysses, dist=dist)

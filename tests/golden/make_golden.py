@@ -8,6 +8,7 @@ function, so the GPU tests can check the CUDA kernels against the reference on
 machines where the reference tree is absent.  Fixtures:
 
   int8_quant.pt   ops/int8_convrot.py:99-111  _dynamic_quant_rows
+  convrot.pt      ops/hadamard.py:35-44       rotate_activation (bf16 and fp16) + _dynamic_quant_rows
   nvfp4.pt        ops/nvfp4.py:124-151        dequantize_nvfp4 of oracle-quantised codes
   rope.pt         ops/rope.py:7-55            rope_rotation_table + rms_rope_apply (44/42/42)
   attention.pt    ops/attention.py:100-131    fusion_attention_bnsd (SDPA host path)
@@ -41,6 +42,20 @@ def make_int8(R) -> dict:
     x = torch.cat([x, torch.zeros(1, 3072), torch.full((1, 3072), 1e-30)], dim=0).to(torch.bfloat16)
     q, s = R.int8_convrot._dynamic_quant_rows(x.to(torch.bfloat16))
     return {"x": x, "q": q, "scale": s}
+
+
+def make_convrot(R) -> dict:
+    """The reference's online rotation (a 16-bit torch.mm against its regular
+    Hadamard matrix) followed by its row quantiser, for bf16 and fp16 input."""
+    g = torch.Generator().manual_seed(5)
+    x = outlier_activations(g, 16, 3072)
+    out = {}
+    for name, dt in (("bf16", torch.bfloat16), ("f16", torch.float16)):
+        xd = x.to(dt)
+        rot = R.hadamard.rotate_activation(xd, 256)
+        q, s = R.int8_convrot._dynamic_quant_rows(rot)
+        out.update({f"x_{name}": xd, f"rot_{name}": rot, f"q_{name}": q, f"scale_{name}": s})
+    return out
 
 
 def make_nvfp4(R) -> dict:
@@ -159,6 +174,7 @@ def main() -> None:
     torch.set_num_threads(1)
     fixtures = {
         "int8_quant.pt": make_int8(R),
+        "convrot.pt": make_convrot(R),
         "nvfp4.pt": make_nvfp4(R),
         "rope.pt": make_rope(R),
         "attention.pt": make_attention(R),

@@ -32,6 +32,9 @@ def test_library_exports_every_symbol():
 
 @pytest.mark.parametrize("name,args,code", [
     ("h3b_quant_i8_rows", (None, 0, 4, 64, 64, None, None, None), 8),
+    ("h3b_quant_i8_rows_convrot", (16, 0, 4, 3072, 3072, 128, 16, 16, None, None), 1),     # group 128
+    ("h3b_quant_i8_rows_convrot", (16, 0, 4, 1000, 1000, 256, 16, 16, None, None), 1),     # k % 256
+    ("h3b_quant_i8_rows_convrot", (16, 0, 4, 24576, 24576, 256, 16, 16, None, None), 1),   # k > 12288
     ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 0, 4, 48, 128, None), 1),  # n%32
     ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 0, 4, 64, 100, None), 1),  # k%128
     ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 2, 4, 64, 128, None), 8),  # gate

@@ -95,3 +95,61 @@ def test_amax_and_zero_input(cuda):
     got = ops.quant_nvfp4(z.to(cuda), hi_first=True)
     want = O.nvfp4_quantize(z, hi_first=True)
     assert got.gs.item() == 1.0 and torch.equal(got.codes.cpu(), want["codes"]) and torch.equal(got.sf.cpu(), want["sf"])
+
+
+# ---------------------------------------------------------------- ConvRot
+
+def test_convrot_golden(cuda):
+    """Rotated activation and codes vs the reference's rotate_activation +
+    _dynamic_quant_rows: bit-exact for bf16; fp16 rotations within the
+    reference GEMM's own 2-ulp rounding (the oracle pins that)."""
+    from minixmax_h3_b200 import ops
+
+    g = load_golden("convrot.pt")
+    x = g["x_bf16"]
+    rot = torch.empty_like(x, device=cuda)
+    q, s = ops.quant_i8_rows(x.to(cuda), convrot_group=256, x_rot_out=rot)
+    assert torch.equal(rot.cpu(), g["rot_bf16"])
+    assert torch.equal(q.cpu(), g["q_bf16"]) and torch.equal(s.cpu(), g["scale_bf16"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,k", [(1, 256), (37, 3072), (130, 4096), (64, 12288)])
+def test_convrot_bit_exact(cuda, dtype, m, k):
+    from minixmax_h3_b200 import ops
+
+    x = _outliers(m + k, m, k).to(dtype)
+    rot = torch.empty(m, k, dtype=dtype, device=cuda)
+    q, s = ops.quant_i8_rows(x.to(cuda), convrot_group=256, x_rot_out=rot)
+    rot_ref = O.rotate_activation_exact(x, 256)
+    q_ref, s_ref = O.dynamic_quant_rows(rot_ref)
+    assert torch.equal(rot.cpu(), rot_ref)
+    assert torch.equal(q.cpu(), q_ref) and torch.equal(s.cpu(), s_ref)
+
+
+def test_convrot_strided_rows_and_zero(cuda):
+    from minixmax_h3_b200 import ops
+
+    base = _outliers(5, 20, 3072 + 64)
+    base[3] = 0
+    x = base[:, :3072]  # row pitch 3136 elements
+    q, s = ops.quant_i8_rows(x.to(cuda), convrot_group=256)
+    q_ref, s_ref = O.dynamic_quant_rows(O.rotate_activation_exact(x.contiguous(), 256))
+    assert torch.equal(q.cpu(), q_ref) and torch.equal(s.cpu(), s_ref)
+    assert (q[3] == 0).all()
+
+
+def test_convrot_quantlinear(cuda):
+    """QuantLinear with meta convrot: rotated W8A8 output bit-exact to the
+    oracle's emulated linear (rotation, row quantisation, int32 product,
+    fp32 epilogue, one bf16 rounding)."""
+    from minixmax_h3_b200.modules import QuantLinear
+
+    g = torch.Generator().manual_seed(3)
+    x = _outliers(8, 200, 3072)
+    w = torch.randn(512, 3072, generator=g) * 0.02
+    emu = O.EmulatedQuantLinear(w, "int8", convrot=True)
+    ql = QuantLinear.from_quant_tensors(emu.wq, meta={"format": "int8_tensorwise", "convrot": True},
+                                        weight_scale=emu.ws, device=cuda)
+    y = ql(x.to(cuda))
+    assert torch.equal(y.cpu(), emu(x))

@@ -153,3 +153,41 @@ def test_dit_block_golden_bit_exact():
                                   pos=g["pos"], inv_freq=g["inv_freq"], n_t=g["n_t"], n_h=g["n_h"],
                                   linear=_block_linear(params, g["fmt"]), attn_fp32=False)
         assert torch.equal(out, g["out"]), name
+
+
+# ---------------------------------------------------------------- ConvRot
+
+def test_hadamard_matrix_matches_reference(ref):
+    for size in (4, 16, 64, 256):
+        h_ref = ref.hadamard.build_hadamard(size, torch.device("cpu"), torch.float64).numpy()
+        assert np.array_equal(O.hadamard_matrix(size), h_ref)
+
+
+def test_rotation_matches_reference(ref):
+    """The exact, singly rounded rotation against the reference's 16-bit
+    torch.mm: identical for bf16; for fp16 the reference's CPU GEMM is not
+    correctly rounded in a few elements (at most 2 ulp)."""
+    x = _outliers(11, 64, 3072)
+    for dt, max_ulp, max_frac in ((torch.bfloat16, 0, 0.0), (torch.float16, 2, 2e-4)):
+        xd = x.to(dt)
+        a = O.rotate_activation_exact(xd, 256)
+        b = ref.hadamard.rotate_activation(xd, 256)
+        ulp = (a.view(torch.int16).int() - b.view(torch.int16).int()).abs()
+        assert int(ulp.max()) <= max_ulp
+        assert (ulp > 0).float().mean().item() <= max_frac
+
+
+def test_convrot_golden():
+    g = load_golden("convrot.pt")
+    for name, max_ulp in (("bf16", 0), ("f16", 2)):
+        rot = O.rotate_activation_exact(g[f"x_{name}"], 256)
+        ulp = (rot.view(torch.int16).int() - g[f"rot_{name}"].view(torch.int16).int()).abs()
+        assert int(ulp.max()) <= max_ulp
+    # bf16: rotation and row quantisation bit-exact to the reference's
+    q, s = O.dynamic_quant_rows(O.rotate_activation_exact(g["x_bf16"], 256))
+    assert torch.equal(q, g["q_bf16"]) and torch.equal(s, g["scale_bf16"])
+
+
+def test_rotation_is_orthonormal():
+    h = O.hadamard_matrix(256)
+    assert np.allclose(h @ h.T, np.eye(256), atol=1e-12)
