@@ -54,7 +54,8 @@ enum { H3B_BF16 = 0, H3B_F16 = 1 };
 enum {
   H3B_EPI_STORE = 0,    /* y = acc*scales (+ bias)                            */
   H3B_EPI_GELU = 1,     /* y = gelu_erf(acc*scales (+ bias))                  */
-  H3B_EPI_GATE_RES = 2  /* y[m,n] = resid[m,n] + (acc*scales (+bias)) * gate[n] */
+  H3B_EPI_GATE_RES = 2, /* y[m,n] = resid[m,n] + (acc*scales (+bias)) * gate[n] */
+  H3B_EPI_SWIGLU = 3    /* y[m,j] = silu(g)*u of a row-interleaved fc1, see below */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -107,6 +108,12 @@ H3B_API int h3b_quant_i8_rows_convrot(const void* x, int x_dtype, int64_t m, int
  * y[m,n] = resid[m,n] + v * gate[row_sel[m]*gate_ld + n]; resid is bf16 with
  * row stride ldy and may alias y; row_sel (int32 [m]) may be NULL (row 0);
  * rows with row_sel < 0 keep resid unchanged (tokens outside every segment).
+ * H3B_EPI_SWIGLU (the fc1 -> _swiglu step of model/dit.py:120-129, 298-301):
+ * the weight rows are interleaved in blocks of 32 (rows 64b..64b+31 = gate
+ * outputs 32b.., rows 64b+32..64b+63 = up outputs 32b..); y is [m, n/2] and
+ * y[m,j] = bf16(bf16(silu(g)) * u) with g, u the bf16-rounded outputs of the
+ * gate and up rows, the rounding chain of the reference's unfused
+ * F.silu(gate) * up.  Needs n % 64 == 0.
  * amax_out (optional, caller-zeroed fp32) receives max |y| over the output.
  * k % 128 == 0, n % 32 == 0, ldy % 8 == 0.
  */

@@ -29,7 +29,7 @@ import torch.nn.functional as F
 from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantLinear, RMSNorm
-from .ops import EPI_GATE_RES, EPI_GELU
+from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
 from .ulysses import all_to_all_heads, all_to_all_qkv, clip_mod_segments, split_range
 
 
@@ -211,13 +211,11 @@ class MLP(nn.Module):
         amax_h = global_amax_(amax_h, self.fc1)
         if self.act == "gelu":
             u = self.fc1.forward_fused(h, amax=amax_h, epilogue=EPI_GELU, amax_out=amax_u)
-            global_amax_(amax_u, self.fc2)
         else:
-            g, up = self.fc1.forward_fused(h, amax=amax_h).chunk(2, dim=-1)
-            u = (F.silu(g) * up).contiguous()
-            amax_u = None
-            if self.fc2.quant_format == "nvfp4" and is_distributed():
-                amax_u = global_amax_(ops.amax(u), self.fc2)
+            # silu(gate) * up fused into the fc1 epilogue over the interleaved weight
+            self.fc1.interleave_swiglu()
+            u = self.fc1.forward_fused(h, amax=amax_h, epilogue=EPI_SWIGLU, amax_out=amax_u)
+        global_amax_(amax_u, self.fc2)
         if resid is not None:
             return self.fc2.forward_fused(u, amax=amax_u, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
                                           row_sel=row_sel)

@@ -14,8 +14,6 @@
 
 namespace {
 
-H3B_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
 // One warp per (token, head) row of 128 bf16: lane l owns d = 4l..4l+3.
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t s_len, int heads, int64_t seq_stride,

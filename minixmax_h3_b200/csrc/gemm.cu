@@ -298,6 +298,75 @@ __global__ void __launch_bounds__(THREADS, 1)
         row_scale = (*args.a_gs) * (*args.w_gs);
       }
       const uint32_t t_row = tmem_base + buf * ACC_STRIDE + (static_cast<uint32_t>(quad * 32) << 16);
+      // acc -> fp32 output of column `col` before any activation.  Explicit
+      // _rn ops: no FMA contraction, so the INT8 epilogue is bit-reproducible
+      // as (acc*xs)*ws + bias in fp32.
+      auto dequant = [&](uint32_t raw, int col) -> float {
+        float a;
+        if constexpr (KIND == KIND_I8) {
+          a = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(raw)), row_scale), __ldg(args.ws + col));
+        } else {
+          a = __fmul_rn(__uint_as_float(raw), row_scale);
+        }
+        if (args.bias != nullptr) a = __fadd_rn(a, __bfloat162float(args.bias[col]));
+        return a;
+      };
+      // Stage a 32x32 bf16 block and TMA-store it at output column ocol.  A
+      // staging buffer is reused every other block: first wait until at most
+      // one store (the other buffer's) may still be reading shared memory.
+      auto store_block = [&](const float (&v)[32], int ocol) {
+        uint8_t* sb = out_stage + (stage_seq & 1) * OUT_STAGE_BYTES;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int j = q4 * 8;
+          const uint4 pk = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                      pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+          *reinterpret_cast<uint4*>(sb + swz64(lane, q4)) = pk;
+          if (args.amax_out != nullptr && row_ok) {
+            const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_y, sb, ocol, m0 + quad * 32);  // rows >= m are clipped by the map
+          bulk_commit_group();
+        }
+        ++stage_seq;
+      };
+      if (args.epilogue == H3B_EPI_SWIGLU) {
+        // Column pair p: gate rows n0+64p .. +31 and up rows n0+64p+32 .. +63
+        // of the interleaved weight -> output columns (n0 + 64p)/2 .. +31.
+        for (int p = 0; p < BN / 64; ++p) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32p(t_row + p * 64, rg);
+          tmem_ld32p(t_row + p * 64 + 32, ru);
+          tc_wait_ld();
+          reg_fence32(rg);
+          reg_fence32(ru);
+          if (p == BN / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(&bars->acc_empty[buf]);
+          }
+          const int gcol = n0 + p * 64;
+          if (gcol >= args.n) continue;  // warp-uniform
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float g = bf16r(dequant(rg[j], gcol + j));
+            const float u = bf16r(dequant(ru[j], gcol + 32 + j));
+            const float sg = bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+            v[j] = __fmul_rn(sg, u);
+          }
+          store_block(v, gcol / 2);
+        }
+        continue;
+      }
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32p(t_row + c * 32, r);
@@ -320,19 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          // Explicit _rn ops: no FMA contraction, so the INT8 epilogue is
-          // bit-reproducible as (acc*xs)*ws + bias in fp32.
-          float a;
-          if constexpr (KIND == KIND_I8) {
-            a = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), row_scale),
-                          __ldg(args.ws + col0 + j));
-          } else {
-            a = __fmul_rn(__uint_as_float(r[j]), row_scale);
-          }
-          if (args.bias != nullptr) a = __fadd_rn(a, __bfloat162float(args.bias[col0 + j]));
-          v[j] = a;
-        }
+        for (int j = 0; j < 32; ++j) v[j] = dequant(r[j], col0 + j);
         if (args.epilogue == H3B_EPI_GELU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
@@ -351,32 +408,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
-        // Stage the 32x32 bf16 block and TMA-store it.  A staging buffer is
-        // reused every other block: first wait until at most one store (the
-        // other buffer's) may still be reading shared memory.
-        uint8_t* sb = out_stage + (stage_seq & 1) * OUT_STAGE_BYTES;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int j = q4 * 8;
-          const uint4 pk = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                                      pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
-          *reinterpret_cast<uint4*>(sb + swz64(lane, q4)) = pk;
-          if (args.amax_out != nullptr && row_ok) {
-            const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_y, sb, col0, m0 + quad * 32);  // rows >= m are clipped by the map
-          bulk_commit_group();
-        }
-        ++stage_seq;
+        store_block(v, col0);
       }
     }
     if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
@@ -407,8 +439,9 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
   if (args.out_mode == OUT_BF16) {
-    // y viewed as [m rows, n cols] bf16 with row pitch ldy; 32x32 boxes.
-    rc = h3b::encode_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, args.y, args.n, args.m, args.ldy * 2, 32, 32,
+    // y viewed as [m rows, n (n/2 for SwiGLU) cols] bf16 with row pitch ldy; 32x32 boxes.
+    const int out_cols = args.epilogue == H3B_EPI_SWIGLU ? args.n / 2 : args.n;
+    rc = h3b::encode_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, args.y, out_cols, args.m, args.ldy * 2, 32, 32,
                         CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != H3B_OK) return rc;
   } else {
@@ -446,8 +479,9 @@ extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* 
   if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr || y == nullptr) return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 128);
   if (rc != H3B_OK) return rc;
-  if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
-  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_SWIGLU) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_SWIGLU && (n % 64) != 0) return H3B_ERR_SHAPE;
+  if (ldy < (epilogue == H3B_EPI_SWIGLU ? n / 2 : n) || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
   if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(y)) return H3B_ERR_ALIGN;
   if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
@@ -497,8 +531,9 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
     return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 256);
   if (rc != H3B_OK) return rc;
-  if (ldy < n || (ldy % 8) != 0) return H3B_ERR_SHAPE;
-  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_GATE_RES) return H3B_ERR_ARG;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_SWIGLU) return H3B_ERR_ARG;
+  if (epilogue == H3B_EPI_SWIGLU && (n % 64) != 0) return H3B_ERR_SHAPE;
+  if (ldy < (epilogue == H3B_EPI_SWIGLU ? n / 2 : n) || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
   if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(y) || !h3b::aligned16(a_sf) ||
       !h3b::aligned16(w_sf))

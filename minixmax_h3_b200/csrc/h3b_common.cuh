@@ -357,6 +357,8 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t m, uint32_t n) {
 // ----------------------------------------------------------------------------
 // Small numeric helpers
 // ----------------------------------------------------------------------------
+// fp32 -> nearest-even bf16 -> fp32 (one rounding step of a bf16 computation).
+H3B_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 H3B_DEV float bf16lo_to_f32(uint32_t v) { return __uint_as_float(v << 16); }
 H3B_DEV float bf16hi_to_f32(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

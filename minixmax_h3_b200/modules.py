@@ -89,6 +89,7 @@ class QuantLinear(nn.Module):
         self.register_buffer("pre_quant_scale", None, persistent=False)
         self.weight_layout = "nk"
         self._w_nvfp4: Optional[NVFP4Tensor] = None
+        self._row_perm: Optional[torch.Tensor] = None  # set by interleave_swiglu
 
     @classmethod
     def from_quant_tensors(cls, weight: torch.Tensor, *, meta: dict[str, Any],
@@ -139,6 +140,7 @@ class QuantLinear(nn.Module):
             raise ValueError(f"unsupported quant format: {self.quant_format}")
         self.weight_layout = "nk"
         self._w_nvfp4 = None
+        self._row_perm = None
         if bias is not None:
             self.bias = nn.Parameter(bias.to(device=device, dtype=self._compute_dtype), requires_grad=False)
         if pre_quant_scale is not None:
@@ -157,6 +159,30 @@ class QuantLinear(nn.Module):
             self._w_nvfp4 = NVFP4Tensor(codes, self.weight_scale, self.weight_scale_2, self.out_features,
                                         self.in_features, hi_first=False)
             self.weight_layout = "nk_lo_first"
+
+    def interleave_swiglu(self) -> None:
+        """One-time reorder of an fc1 weight (rows = [gate; up]) into the
+        32-row interleave the fused SwiGLU epilogue reads (ops.swiglu_
+        interleave_perm): codes, per-row scales, block scales and bias move
+        together.  forward() restores the reference's column order; use
+        forward_fused(epilogue=EPI_SWIGLU) for the fused activation."""
+        if self._row_perm is not None:
+            return
+        perm = ops.swiglu_interleave_perm(self.out_features, device=self.weight_scale.device)
+        if self.quant_format == "int8_tensorwise":
+            self.weight_i8 = self.weight_i8[perm].contiguous()
+            self.weight_scale = self.weight_scale[perm].contiguous()
+        elif self.quant_format == "nvfp4":
+            self.weight_u8 = self.weight_u8[perm].contiguous()
+            self.weight_scale = ops.permute_blocked_rows(self.weight_scale, self.out_features, self.in_features,
+                                                         perm)
+            self._w_nvfp4 = None
+        else:
+            raise RuntimeError("interleave_swiglu needs quantised weights")
+        if self.bias is not None and self.bias.numel():
+            self.bias = nn.Parameter(self.bias.data[perm].contiguous(), requires_grad=False)
+        self._row_perm = perm
+        self._inv_perm = torch.argsort(perm)
 
     def _bias(self, x: torch.Tensor) -> Optional[torch.Tensor]:
         return None if self.bias is None or self.bias.numel() == 0 else self.bias.to(torch.bfloat16)
@@ -193,6 +219,8 @@ class QuantLinear(nn.Module):
         if self.quant_format == "nvfp4" or x2.dtype != torch.float16:
             x2 = x2.to(torch.bfloat16)
         y = self.forward_fused(x2)
+        if self._row_perm is not None:  # interleaved for the fused SwiGLU: reference column order
+            y = y[:, self._inv_perm]
         return y.to(out_dtype).reshape(*lead, self.out_features)
 
 

@@ -13,7 +13,7 @@ import torch
 
 from ._lib import call
 
-EPI_STORE, EPI_GELU, EPI_GATE_RES = 0, 1, 2
+EPI_STORE, EPI_GELU, EPI_GATE_RES, EPI_SWIGLU = 0, 1, 2, 3
 
 
 def _stream(t: torch.Tensor) -> int:
@@ -76,12 +76,14 @@ def gemm_i8(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor
 
     EPI_GATE_RES: y = resid + v * gate[row_sel[m]] with gate a [rows, N] table
     (a strided view is fine) and resid updated in place when out is None.
+    EPI_SWIGLU: w rows interleaved by swiglu_interleave_perm; y is [m, N/2].
     """
     _cuda(q, xs, w, ws, bias, resid, gate, row_sel, amax_out, out)
     m, k = q.shape
     n = w.shape[0]
     if out is None:
-        out = resid if epilogue == EPI_GATE_RES else torch.empty((m, n), dtype=torch.bfloat16, device=q.device)
+        out = resid if epilogue == EPI_GATE_RES else torch.empty(
+            (m, n // 2 if epilogue == EPI_SWIGLU else n), dtype=torch.bfloat16, device=q.device)
     gate_ld = _gate_ld(gate)
     call("h3b_gemm_i8_bf16", q.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), _ptr(bias), out.data_ptr(),
          out.stride(0), _ptr(resid), _ptr(gate), gate_ld, _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k,
@@ -161,6 +163,43 @@ def swap_nibbles(u8: torch.Tensor) -> torch.Tensor:
     return dst
 
 
+def swiglu_interleave_perm(n: int, device=None) -> torch.Tensor:
+    """Row order of an fc1 weight [n = 2*ffn, K] for EPI_SWIGLU: blocks of 32
+    gate rows and the matching 32 up rows alternate, so new row 64b + j is
+    gate row 32b + j and new row 64b + 32 + j is up row ffn + 32b + j
+    (the halves of model/dit.py:120-129 x.chunk(2, dim=-1))."""
+    if n % 64:
+        raise ValueError("SwiGLU fc1 needs 2*ffn % 64 == 0")
+    ffn = n // 2
+    b = torch.arange(ffn // 32).repeat_interleave(32)
+    j = torch.arange(32).repeat(ffn // 32)
+    gate = 32 * b + j
+    perm = torch.stack([gate.view(-1, 32), (ffn + gate).view(-1, 32)], dim=1).reshape(-1)
+    return perm.to(device)
+
+
+def _blocked_index(rows: int, ncols: int, device) -> torch.Tensor:
+    """Flat offsets of every (row, scale column) of the 128x4 blocked scale
+    layout (ops/nvfp4.py from_blocked), rows padded to 128: [rows_pad, ncols]."""
+    rows_pad = (rows + 127) // 128 * 128
+    r = torch.arange(rows_pad, device=device).view(-1, 1)
+    c = torch.arange(ncols, device=device).view(1, -1)
+    ncb = ncols // 4
+    return ((r // 128) * ncb + c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + c % 4
+
+
+def permute_blocked_rows(sf: torch.Tensor, rows: int, k: int, perm: torch.Tensor) -> torch.Tensor:
+    """Reorders the rows of NVFP4 block scales kept in the blocked layout
+    (row i of the result = row perm[i]); padding rows stay zero."""
+    ncols = k // 16
+    idx = _blocked_index(rows, ncols, sf.device)
+    dense = sf.reshape(-1)[idx]
+    full = torch.cat([perm.to(sf.device), torch.arange(rows, idx.shape[0], device=sf.device)])
+    out = torch.zeros_like(sf.reshape(-1))
+    out[idx.reshape(-1)] = dense[full].reshape(-1)
+    return out.view_as(sf)
+
+
 def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = None, *,
                epilogue: int = EPI_STORE, resid: Optional[torch.Tensor] = None,
                gate: Optional[torch.Tensor] = None, row_sel: Optional[torch.Tensor] = None,
@@ -171,7 +210,8 @@ def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = No
     _cuda(a.codes, w.codes, bias, resid, gate, row_sel, amax_out, out)
     m, n, k = a.rows, w.rows, a.k
     if out is None:
-        out = resid if epilogue == EPI_GATE_RES else torch.empty((m, n), dtype=torch.bfloat16, device=a.codes.device)
+        out = resid if epilogue == EPI_GATE_RES else torch.empty(
+            (m, n // 2 if epilogue == EPI_SWIGLU else n), dtype=torch.bfloat16, device=a.codes.device)
     call("h3b_gemm_nvfp4_bf16", a.codes.data_ptr(), a.sf.data_ptr(), a.gs.data_ptr(), w.codes.data_ptr(),
          w.sf.data_ptr(), w.gs.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0), _ptr(resid), _ptr(gate),
          _gate_ld(gate), _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k, _stream(a.codes))

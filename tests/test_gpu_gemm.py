@@ -117,3 +117,41 @@ def test_nvfp4_gemm(cuda, m, n, k):
     ad = O.nvfp4_dequantize(a_or["codes"], a_or["gs"], a_or["sf"], k, False).to(torch.bfloat16)
     wd = O.nvfp4_dequantize(w_or["codes"], w_or["gs"], w_or["sf"], k, False).to(torch.bfloat16)
     assert_close_bf16(y, F.linear(ad, wd, bias).float(), max_abs=5e-2)
+
+
+def _bf16_ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return (a.view(torch.int16).int() - b.view(torch.int16).int()).abs()
+
+
+@pytest.mark.parametrize("fmt", ["int8", "nvfp4"])
+@pytest.mark.parametrize("m,ffn,k", [(200, 224, 512), (130, 1536, 3072)])
+def test_swiglu_epilogue(cuda, fmt, m, ffn, k):
+    """fc1 with the fused SwiGLU epilogue vs the reference's unfused chain on
+    the same accumulators: STORE the [m, 2*ffn] bf16 output, then
+    F.silu(gate) * up in bf16 (model/dit.py:120-129).  The two silu
+    evaluations may differ in the last fp32 bit; allow 1 bf16 ulp in <0.1%."""
+    from minixmax_h3_b200 import ops
+    from minixmax_h3_b200.modules import QuantLinear
+
+    g = torch.Generator().manual_seed(m + ffn)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(cuda)
+    w = torch.randn(2 * ffn, k, generator=g) * 0.05
+    if fmt == "int8":
+        wq, ws = O.quantize_weight_int8(w)
+        ql = QuantLinear.from_quant_tensors(wq, meta={"format": "int8_tensorwise"}, weight_scale=ws, device=cuda)
+    else:
+        qz = O.nvfp4_quantize(w.to(torch.bfloat16), hi_first=True)
+        ql = QuantLinear.from_quant_tensors(qz["codes"], meta={"format": "nvfp4"}, weight_scale=qz["sf"],
+                                            weight_scale_2=qz["gs"], device=cuda)
+    full = ql.forward_fused(x)                       # [m, 2*ffn], reference column order
+    gate, up = full.chunk(2, dim=-1)
+    want = (F.silu(gate) * up)
+    ql.interleave_swiglu()
+    amax = torch.zeros(1, dtype=torch.float32, device=cuda)
+    got = ql.forward_fused(x, epilogue=ops.EPI_SWIGLU, amax_out=amax)
+    assert got.shape == (m, ffn)
+    ulp = _bf16_ulps(got, want)
+    assert int(ulp.max()) <= 1 and (ulp > 0).float().mean().item() < 1e-3
+    assert amax.item() == got.float().abs().max().item()
+    # the plain forward still returns the reference's [gate | up] column order
+    assert torch.equal(ql(x), full)
