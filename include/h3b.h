@@ -238,6 +238,57 @@ H3B_API int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidd
 H3B_API int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidden, int64_t ld, const void* gate,
                               int64_t tab_ld, const int32_t* row_sel, h3b_stream_t stream);
 
+/* ------------------------------------------------- Ulysses P2P exchange */
+
+/*
+ * CUDA IPC registration of the exchange buffers (the receive buffers of the
+ * P2P Ulysses path; the reference allocates its SP buffers once and reuses
+ * them, runtime/dist.py:30,172-203).  h3b_ipc_export writes the 64-byte IPC
+ * handle of the allocation holding dev_ptr and dev_ptr's byte offset in it;
+ * a peer process passes both to h3b_ipc_import to map the same memory
+ * (*dev_ptr = mapped base + offset) and to h3b_ipc_close to unmap it.
+ * Setup-time calls, not for the step loop.
+ */
+H3B_API int h3b_ipc_export(const void* dev_ptr, uint8_t* handle64, int64_t* offset);
+H3B_API int h3b_ipc_import(const uint8_t* handle64, int64_t offset, void** dev_ptr);
+H3B_API int h3b_ipc_close(void* dev_ptr, int64_t offset);
+
+/*
+ * QKV projection fused with the sequence->head all-to-all (ops/ulysses.py:
+ * 14-30 applied to the qkv_proj output of model/dit.py:169-190): the GEMM of
+ * h3b_gemm_i8_bf16 / h3b_gemm_nvfp4_bf16 with n = 3*heads*128, whose output
+ * column (part, head, d) of local row t is stored to rank
+ * head / (heads/world_size)'s receive buffer recv_bufs[r] — laid out
+ * [world_size*m, 3, heads/world_size, 128] bf16 — at row rank*m + t.
+ * recv_bufs: world_size device pointers valid in this process (own buffer
+ * and IPC-imported peers').  No activation or residual epilogue.  The
+ * caller orders the exchange (all ranks' launches complete) before reading
+ * a receive buffer, e.g. with a collective on the same stream.
+ */
+H3B_API int h3b_gemm_i8_seq2head(const int8_t* q, const float* xs, const int8_t* w, const float* ws,
+                                 const void* bias, void* const* recv_bufs, int64_t world_size, int64_t rank,
+                                 int64_t heads, int64_t m, int64_t n, int64_t k, h3b_stream_t stream);
+H3B_API int h3b_gemm_nvfp4_seq2head(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                    const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs,
+                                    const void* bias, void* const* recv_bufs, int64_t world_size, int64_t rank,
+                                    int64_t heads, int64_t m, int64_t n, int64_t k, h3b_stream_t stream);
+
+/*
+ * Attention fused with the head->sequence all-to-all (ops/ulysses.py:32-41
+ * on the attention output, model/dit.py:248-289): h3b_attention_fwd over
+ * this rank's `heads` local heads and all s_q = world_size*s_local tokens,
+ * writing query row t of local head h into o_bufs[t / s_local] (rank
+ * t/s_local's out-projection input, [s_local, H, 128] with strides
+ * o_seq_stride / o_head_stride elements) at row t % s_local, head head0 + h.
+ * Same ordering contract as h3b_gemm_*_seq2head.
+ */
+H3B_API int h3b_attention_fwd_head2seq(const void* q, const void* k, const void* v, void* const* o_bufs,
+                                       int64_t world_size, int64_t s_local, int64_t head0, int64_t o_seq_stride,
+                                       int64_t o_head_stride, float* amax_out, int64_t heads, int64_t s_q,
+                                       int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
+                                       int64_t kv_seq_stride, int64_t kv_head_stride, float scale,
+                                       h3b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,12 @@ SIGNATURES: dict[str, list] = {
                             c_ptr, c_ptr, c_int, c_i64, c_i64, c_i64, c_ptr],
     "h3b_attention_fwd": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                           c_i64, c_i64, c_f32, c_ptr],
+    "h3b_ipc_export": [c_ptr, c_ptr, c_ptr],
+    "h3b_ipc_import": [c_ptr, c_i64, c_ptr],
+    "h3b_ipc_close": [c_ptr, c_i64],
+    "h3b_gemm_i8_seq2head": [c_ptr] * 6 + [c_i64] * 6 + [c_ptr],
+    "h3b_gemm_nvfp4_seq2head": [c_ptr] * 8 + [c_i64] * 6 + [c_ptr],
+    "h3b_attention_fwd_head2seq": [c_ptr] * 4 + [c_i64] * 5 + [c_ptr] + [c_i64] * 7 + [c_f32, c_ptr],
     "h3b_qk_rmsnorm_rope": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_f32, c_ptr, c_i64, c_ptr,
                             c_int, c_int, c_ptr],
     "h3b_rmsnorm_modulate": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_f32, c_ptr,

@@ -30,7 +30,8 @@ from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
-from .ulysses import all_to_all_heads, all_to_all_qkv, clip_mod_segments, split_range
+from .ulysses import (all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer, phase_barrier,
+                      split_range, transport)
 
 
 @dataclass
@@ -157,6 +158,8 @@ class Attention(nn.Module):
         otherwise returns attn(h)."""
         s_local = h.shape[0]
         sp = self.sequence_parallel and is_distributed()
+        if sp and transport() == "p2p":
+            return self._forward_p2p(h, rope_freqs, amax_h=amax_h, resid=resid, gate=gate, row_sel=row_sel)
         qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
         if rope_freqs is not None:
@@ -184,6 +187,44 @@ class Attention(nn.Module):
             o = ATTN_TIMER.record(lambda: ops.attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5,
                                                         amax_out=amax_o), flops)
             o = o.view(s_local, self.heads * self.head_dim)
+        if resid is not None:
+            return self.out_proj.forward_fused(o, amax=amax_o, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
+                                               row_sel=row_sel)
+        return self.out_proj.forward_fused(o, amax=amax_o)
+
+
+    def _forward_p2p(self, h: torch.Tensor, rope_freqs: Optional[RopeSpec], *, amax_h=None, resid=None,
+                     gate=None, row_sel=None) -> torch.Tensor:
+        """Sequence-parallel attention with both Ulysses exchanges fused into
+        kernels: the QKV GEMM stores into the head owners' receive buffers, the
+        attention stores into the token owners' out-projection inputs.  Each
+        phase ends with a collective on the compute stream (see
+        ulysses.phase_barrier); RMSNorm + RoPE run after the exchange on the
+        full sequence (per-token, per-head: the same values as before it)."""
+        st = state()
+        ws, rank = st.world_size, st.rank
+        s_local = h.shape[0]
+        hl = self.heads // ws
+        s_full = s_local * ws
+        recv = peer_buffer("ulysses_qkv", (s_full, 3, hl, self.head_dim), torch.bfloat16, h.device)
+        obuf = peer_buffer("ulysses_o", (s_local, self.heads, self.head_dim), torch.bfloat16, h.device)
+        self.qkv_proj.forward_seq2head(h, recv.ptrs, rank, self.heads, amax=global_amax_(amax_h, self.qkv_proj))
+        phase_barrier(h.device)
+        q, k, v = recv.local[:, 0], recv.local[:, 1], recv.local[:, 2]
+        if rope_freqs is not None:
+            ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, rope_freqs.pos, 0,
+                                rope_freqs.inv_freq, rope_freqs.n_t, rope_freqs.n_h)
+        else:
+            zeros = torch.zeros(64, dtype=torch.float32, device=h.device)
+            pos0 = torch.zeros(s_full, 3, dtype=torch.float32, device=h.device)
+            ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, pos0, 0, zeros, 64, 0)
+        amax_o = torch.zeros(1, dtype=torch.float32, device=h.device)
+        flops = 4.0 * s_full * s_full * self.head_dim * hl
+        ATTN_TIMER.record(lambda: ops.attention_head2seq(q, k, v, obuf.ptrs, s_local=s_local, head0=rank * hl,
+                                                         total_heads=self.heads, scale=self.head_dim ** -0.5,
+                                                         amax_out=amax_o), flops)
+        phase_barrier(h.device, amax_o)  # orders the O stores; amax_o is now the global max
+        o = obuf.local.view(s_local, self.heads * self.head_dim)
         if resid is not None:
             return self.out_proj.forward_fused(o, amax=amax_o, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
                                                row_sel=row_sel)

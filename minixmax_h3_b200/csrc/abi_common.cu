@@ -1,7 +1,9 @@
 // Library-wide C-ABI pieces: version, device status aggregation, tensor-map
-// encoding through cudaGetDriverEntryPoint, SM-count cache.
+// encoding through cudaGetDriverEntryPoint, SM-count cache, and the CUDA IPC
+// registration of peer buffers for the P2P Ulysses exchange.
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -89,4 +91,54 @@ extern "C" int h3b_device_status(int32_t* out4, int clear) {
     }
   }
   return H3B_OK;
+}
+
+// ---------------------------------------------------------------- CUDA IPC
+namespace {
+
+using PFN_addr_range = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+PFN_addr_range addr_range_fn() {
+  static PFN_addr_range fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_addr_range>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+extern "C" int h3b_ipc_export(const void* dev_ptr, uint8_t* handle64, int64_t* offset) {
+  if (dev_ptr == nullptr || handle64 == nullptr || offset == nullptr) return H3B_ERR_ARG;
+  auto range = addr_range_fn();
+  if (range == nullptr) return H3B_ERR_LAUNCH;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return H3B_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return H3B_ERR_LAUNCH;
+  static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+  memcpy(handle64, &h, 64);
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return H3B_OK;
+}
+
+extern "C" int h3b_ipc_import(const uint8_t* handle64, int64_t offset, void** dev_ptr) {
+  if (handle64 == nullptr || dev_ptr == nullptr || offset < 0) return H3B_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, 64);
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return H3B_ERR_LAUNCH;
+  *dev_ptr = static_cast<uint8_t*>(base) + offset;
+  return H3B_OK;
+}
+
+extern "C" int h3b_ipc_close(void* dev_ptr, int64_t offset) {
+  if (dev_ptr == nullptr || offset < 0) return H3B_ERR_ARG;
+  return cudaIpcCloseMemHandle(static_cast<uint8_t*>(dev_ptr) - offset) == cudaSuccess ? H3B_OK : H3B_ERR_LAUNCH;
 }

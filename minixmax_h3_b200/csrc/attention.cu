@@ -24,6 +24,11 @@
 // PV_i(j-1), so when a softmax sees S_i(j) ready, O_i is settled.
 // The row max is rescaled lazily: O and the row sum are corrected only when
 // the running max grows by more than 8 (log2 domain), which bounds P by 2^8.
+// Head->sequence scatter (h3b_attention_fwd_head2seq, the Ulysses exchange
+// of ops/ulysses.py:32-41 fused into the epilogue): query row t of local head
+// h is written to rank t / s_local's out-projection input [s_local, H, 128]
+// at row t % s_local, global head head0 + h, through that rank's buffer
+// pointer (this GPU's own or a peer's, mapped by CUDA IPC).
 // Q/K tiles are K-major and V tiles MN-major, all with the 128-byte swizzle,
 // loaded by non-multicast TMA from any (seq, head) strides.  Every wait is
 // bounded, and every parity wait is at most one phase behind its barrier
@@ -77,8 +82,14 @@ struct __align__(8) Bars {
 
 constexpr size_t SMEM_BYTES = 1024 + 2 * Q_TILE_BYTES + KST * KV_TILE_BYTES + VST * KV_TILE_BYTES + sizeof(Bars);
 
+constexpr int MAX_PEERS = 8;
+
 struct AttnArgs {
   __nv_bfloat16* o;
+  __nv_bfloat16* o_peers[MAX_PEERS];  // head->seq scatter destinations (peer_mode)
+  int peer_mode;
+  int s_local;
+  int head0;
   float* lse;
   float* amax_out;
   int64_t o_seq_stride;
@@ -448,8 +459,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int q_row = q0 + wg * BQ + row;
       const float inv_l = 1.0f / l_run;
       float o_amax = 0.0f;
-      __nv_bfloat16* orow = args.o + static_cast<int64_t>(q_row) * args.o_seq_stride +
-                            static_cast<int64_t>(head) * args.o_head_stride;
+      __nv_bfloat16* orow;
+      if (args.peer_mode) {
+        const int dst = q_row < args.s_q ? q_row / args.s_local : 0;
+        orow = args.o_peers[dst] + static_cast<int64_t>(q_row - dst * args.s_local) * args.o_seq_stride +
+               static_cast<int64_t>(args.head0 + head) * args.o_head_stride;
+      } else {
+        orow = args.o + static_cast<int64_t>(q_row) * args.o_seq_stride +
+               static_cast<int64_t>(head) * args.o_head_stride;
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
@@ -478,6 +496,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (args.lse != nullptr && q_row < args.s_q) {
         args.lse[static_cast<int64_t>(head) * args.s_q + q_row] = (m_run + __log2f(l_run)) * 0.69314718055994531f;
       }
+      if (args.peer_mode) __threadfence_system();  // peer writes visible system-wide
     }
   }
 
@@ -491,20 +510,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 }  // namespace
 
-extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, float* amax_out,
-                                 int64_t heads,
-                                 int64_t s_q, int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
-                                 int64_t kv_seq_stride, int64_t kv_head_stride, int64_t o_seq_stride,
-                                 int64_t o_head_stride, float scale, h3b_stream_t stream) {
-  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return H3B_ERR_ARG;
+namespace {
+
+int launch_attention(const void* q, const void* k, const void* v, AttnArgs a, int64_t heads, int64_t s_q,
+                     int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride, int64_t kv_seq_stride,
+                     int64_t kv_head_stride, float scale, cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr) return H3B_ERR_ARG;
   if (heads <= 0 || s_q <= 0 || s_kv <= 0 || heads > 65535 || s_q > (1ll << 30) || s_kv > (1ll << 30))
     return H3B_ERR_SHAPE;
   if (!(scale > 0.0f)) return H3B_ERR_ARG;
-  const int64_t strides[6] = {q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride, o_seq_stride,
-                              o_head_stride};
+  const int64_t strides[6] = {q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride, a.o_seq_stride,
+                              a.o_head_stride};
   for (int64_t st : strides)
     if (st <= 0 || (st % 8) != 0) return H3B_ERR_ALIGN;
-  if (!h3b::aligned16(q) || !h3b::aligned16(k) || !h3b::aligned16(v) || !h3b::aligned16(o)) return H3B_ERR_ALIGN;
+  if (!h3b::aligned16(q) || !h3b::aligned16(k) || !h3b::aligned16(v)) return H3B_ERR_ALIGN;
   CUtensorMap tq, tk, tv;
   int rc = h3b::encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, D, s_q, heads, q_seq_stride * 2,
                           q_head_stride * 2, 64, BQ, 1, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -523,16 +542,55 @@ extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, vo
       return H3B_ERR_LAUNCH;
     attr = true;
   }
-  AttnArgs a;
+  a.s_q = static_cast<int>(s_q);
+  a.s_kv = static_cast<int>(s_kv);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
+  attention_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, a);
+  return h3b::launch_status();
+}
+
+}  // namespace
+
+extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, float* amax_out,
+                                 int64_t heads,
+                                 int64_t s_q, int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
+                                 int64_t kv_seq_stride, int64_t kv_head_stride, int64_t o_seq_stride,
+                                 int64_t o_head_stride, float scale, h3b_stream_t stream) {
+  if (o == nullptr) return H3B_ERR_ARG;
+  if (!h3b::aligned16(o)) return H3B_ERR_ALIGN;
+  AttnArgs a{};
   a.o = static_cast<__nv_bfloat16*>(o);
   a.lse = lse;
   a.amax_out = amax_out;
   a.o_seq_stride = o_seq_stride;
   a.o_head_stride = o_head_stride;
-  a.s_q = static_cast<int>(s_q);
-  a.s_kv = static_cast<int>(s_kv);
-  a.scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
-  attention_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, a);
-  return h3b::launch_status();
+  return launch_attention(q, k, v, a, heads, s_q, s_kv, q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride,
+                          scale, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_attention_fwd_head2seq(const void* q, const void* k, const void* v, void* const* o_bufs,
+                                          int64_t world_size, int64_t s_local, int64_t head0, int64_t o_seq_stride,
+                                          int64_t o_head_stride, float* amax_out, int64_t heads, int64_t s_q,
+                                          int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride,
+                                          int64_t kv_seq_stride, int64_t kv_head_stride, float scale,
+                                          h3b_stream_t stream) {
+  if (o_bufs == nullptr) return H3B_ERR_ARG;
+  if (world_size < 1 || world_size > MAX_PEERS || s_local <= 0 || s_q != world_size * s_local || head0 < 0)
+    return H3B_ERR_SHAPE;
+  AttnArgs a{};
+  for (int64_t r = 0; r < world_size; ++r) {
+    if (o_bufs[r] == nullptr) return H3B_ERR_ARG;
+    if (!h3b::aligned16(o_bufs[r])) return H3B_ERR_ALIGN;
+    a.o_peers[r] = static_cast<__nv_bfloat16*>(o_bufs[r]);
+  }
+  a.o = a.o_peers[0];
+  a.peer_mode = 1;
+  a.s_local = static_cast<int>(s_local);
+  a.head0 = static_cast<int>(head0);
+  a.amax_out = amax_out;
+  a.o_seq_stride = o_seq_stride;
+  a.o_head_stride = o_head_stride;
+  return launch_attention(q, k, v, a, heads, s_q, s_kv, q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride,
+                          scale, reinterpret_cast<cudaStream_t>(stream));
 }

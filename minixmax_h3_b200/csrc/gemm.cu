@@ -26,6 +26,14 @@
 //          address skips 2 TMEM columns (= 64 rows) for odd tiles.
 // Operands are K-major with the 128-byte swizzle.  No load uses cluster
 // multicast.  Every wait is bounded.
+//
+// Sequence->head scatter (the Ulysses exchange fused into the QKV
+// projection, ops/ulysses.py:14-30 after model/dit.py:169-190): each 32x32
+// output block lies in one (q|k|v, head) slice and is TMA-stored straight
+// into the receive buffer [ws*m, 3, H/ws, 128] of the rank that owns the
+// head, at this rank's rows, through one tensor map per destination whose
+// rows are clipped to this rank's range.  Destinations are this GPU's own
+// buffer or peers' buffers mapped by CUDA IPC (plain stores over NVLink).
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
 
@@ -45,7 +53,12 @@ constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 stagin
 constexpr int ACC_STRIDE = 256;           // TMEM columns between the two accumulators
 
 enum Kind { KIND_I8 = 0, KIND_NVF4 = 1 };
-enum OutMode { OUT_BF16 = 0, OUT_I32 = 1 };
+enum OutMode { OUT_BF16 = 0, OUT_I32 = 1, OUT_SEQ2HEAD = 2 };
+
+constexpr int MAX_PEERS = 8;
+struct PeerMaps {
+  CUtensorMap m[MAX_PEERS];  // per destination rank (OUT_SEQ2HEAD)
+};
 
 struct GemmArgs {
   const float* xs;     // i8: per-row activation scale [m]
@@ -65,6 +78,8 @@ struct GemmArgs {
   int m, n, k;         // k in elements
   int epilogue;
   int out_mode;
+  int heads_per_rank;  // OUT_SEQ2HEAD: H / world_size
+  int hd;              // OUT_SEQ2HEAD: H * 128 (columns per q|k|v part)
 };
 
 template <int KIND>
@@ -119,7 +134,8 @@ H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c
 template <int KIND>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                const __grid_constant__ CUtensorMap tmap_y, const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ PeerMaps peers,
+                const GemmArgs args) {
   using C = Cfg<KIND>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -293,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float gmul = gate_row < 0 ? 0.0f : 1.0f;  // rows outside every segment keep resid
       float row_scale = 1.0f;
       if constexpr (KIND == KIND_I8) {
-        if (args.out_mode == OUT_BF16 && row_ok) row_scale = args.xs[row];
+        if (args.out_mode != OUT_I32 && row_ok) row_scale = args.xs[row];
       } else {
         row_scale = (*args.a_gs) * (*args.w_gs);
       }
@@ -334,7 +350,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmap_y, sb, ocol, m0 + quad * 32);  // rows >= m are clipped by the map
+          if (args.out_mode == OUT_SEQ2HEAD) {
+            const int part = ocol / args.hd, rem = ocol - part * args.hd;
+            const int head = rem >> 7, d0 = rem & 127;
+            const int dst = head / args.heads_per_rank, lh = head - dst * args.heads_per_rank;
+            tma_store_2d(&peers.m[dst], sb, (part * args.heads_per_rank + lh) * 128 + d0, m0 + quad * 32);
+          } else {
+            tma_store_2d(&tmap_y, sb, ocol, m0 + quad * 32);  // rows >= m are clipped by the map
+          }
           bulk_commit_group();
         }
         ++stage_seq;
@@ -411,7 +434,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         store_block(v, col0);
       }
     }
-    if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
+    if (lane == 0) {
+      bulk_wait_group<0>();  // stores complete before the CTA exits
+      if (args.out_mode == OUT_SEQ2HEAD) __threadfence_system();  // peer writes visible system-wide
+    }
     __syncwarp();
     if (args.amax_out != nullptr) {
       y_amax = warp_max(y_amax);
@@ -429,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <int KIND>
 int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
-                cudaStream_t st) {
+                cudaStream_t st, const PeerMaps* peer_maps = nullptr) {
   using C = Cfg<KIND>;
   CUtensorMap ta, tb, ty;
   int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
@@ -445,7 +471,7 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
                         CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != H3B_OK) return rc;
   } else {
-    ty = ta;  // the int32 path stores directly; the map is never used
+    ty = ta;  // the int32 and scatter paths never use this map
   }
   const size_t smem = smem_bytes<KIND>();
   static bool attr_set[2] = {false, false};
@@ -459,7 +485,8 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
   const int n_tiles = static_cast<int>((args.n + C::BN - 1) / C::BN);
   const int tiles = m_tiles * n_tiles;
   const int grid = tiles < h3b::num_sms() ? tiles : h3b::num_sms();
-  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, ty, args);
+  static const PeerMaps no_peers = {};
+  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, ty, peer_maps ? *peer_maps : no_peers, args);
   return h3b::launch_status();
 }
 
@@ -558,4 +585,79 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
   a.epilogue = epilogue;
   a.out_mode = OUT_BF16;
   return launch_gemm<KIND_NVF4>(a_codes, w_codes, k / 2, k / 2, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+// Validates the seq->head scatter arguments and encodes one tensor map per
+// destination rank: recv_bufs[r] + rank*m rows, m rows of 3*(H/ws)*128 bf16.
+int make_seq2head_maps(void* const* recv_bufs, int64_t world_size, int64_t rank, int64_t heads, int64_t m,
+                       int64_t n, PeerMaps* maps, GemmArgs* a) {
+  if (recv_bufs == nullptr) return H3B_ERR_ARG;
+  if (world_size < 1 || world_size > MAX_PEERS || rank < 0 || rank >= world_size) return H3B_ERR_ARG;
+  if (heads <= 0 || heads % world_size != 0 || n != 3 * heads * 128) return H3B_ERR_SHAPE;
+  const int64_t hl = heads / world_size;
+  const int64_t row_elems = 3 * hl * 128;
+  for (int64_t r = 0; r < world_size; ++r) {
+    if (recv_bufs[r] == nullptr || !h3b::aligned16(recv_bufs[r])) return H3B_ERR_ALIGN;
+    const uint8_t* base = static_cast<const uint8_t*>(recv_bufs[r]) + rank * m * row_elems * 2;
+    const int rc = h3b::encode_2d(&maps->m[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, row_elems, m, row_elems * 2,
+                                  32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != H3B_OK) return rc;
+  }
+  a->out_mode = OUT_SEQ2HEAD;
+  a->heads_per_rank = static_cast<int>(hl);
+  a->hd = static_cast<int>(heads * 128);
+  a->epilogue = H3B_EPI_STORE;
+  a->y = recv_bufs[rank];
+  a->ldy = row_elems;
+  return H3B_OK;
+}
+
+}  // namespace
+
+extern "C" int h3b_gemm_i8_seq2head(const int8_t* q, const float* xs, const int8_t* w, const float* ws,
+                                    const void* bias, void* const* recv_bufs, int64_t world_size, int64_t rank,
+                                    int64_t heads, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+  if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr) return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 128);
+  if (rc != H3B_OK) return rc;
+  if (!h3b::aligned16(q) || !h3b::aligned16(w)) return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  PeerMaps maps{};
+  rc = make_seq2head_maps(recv_bufs, world_size, rank, heads, m, n, &maps, &a);
+  if (rc != H3B_OK) return rc;
+  a.xs = xs;
+  a.ws = ws;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  return launch_gemm<KIND_I8>(q, w, k, k, a, reinterpret_cast<cudaStream_t>(stream), &maps);
+}
+
+extern "C" int h3b_gemm_nvfp4_seq2head(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                       const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs,
+                                       const void* bias, void* const* recv_bufs, int64_t world_size, int64_t rank,
+                                       int64_t heads, int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+  if (a_codes == nullptr || a_sf == nullptr || a_gs == nullptr || w_codes == nullptr || w_sf == nullptr ||
+      w_gs == nullptr)
+    return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 256);
+  if (rc != H3B_OK) return rc;
+  if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(a_sf) || !h3b::aligned16(w_sf))
+    return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  PeerMaps maps{};
+  rc = make_seq2head_maps(recv_bufs, world_size, rank, heads, m, n, &maps, &a);
+  if (rc != H3B_OK) return rc;
+  a.a_gs = a_gs;
+  a.w_gs = w_gs;
+  a.a_sf = a_sf;
+  a.w_sf = w_sf;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  return launch_gemm<KIND_NVF4>(a_codes, w_codes, k / 2, k / 2, a, reinterpret_cast<cudaStream_t>(stream), &maps);
 }

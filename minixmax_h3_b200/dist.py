@@ -69,6 +69,9 @@ def init(backend: Optional[str] = None, timeout_s: float = 120.0) -> DistState:
 
 def destroy() -> None:
     global _STATE
+    from .ulysses import release_peer_buffers  # P2P mappings go before the group
+
+    release_peer_buffers()
     if tdist.is_initialized():
         tdist.destroy_process_group()
     _STATE = DistState()

@@ -206,6 +206,22 @@ class QuantLinear(nn.Module):
                                   row_sel=row_sel, amax_out=amax_out, out=out)
         raise RuntimeError("QuantLinear has no quantised weights (call set_quant first)")
 
+    def forward_seq2head(self, x: torch.Tensor, recv_ptrs, rank: int, heads: int, *,
+                         amax: Optional[torch.Tensor] = None) -> None:
+        """QKV projection of this rank's tokens stored straight into every head
+        owner's receive buffer (ops.gemm_*_seq2head): the projection and the
+        seq->head Ulysses exchange in one kernel."""
+        if self.quant_format == "int8_tensorwise":
+            q, xs = ops.quant_i8_rows(x, convrot_group=self.group_size if self.convrot else 0)
+            ops.gemm_i8_seq2head(q, xs, self.weight_i8, self.weight_scale, self._bias(x), recv_ptrs, rank, heads)
+            return
+        if self.quant_format == "nvfp4":
+            self.prepare_cube()
+            a = ops.quant_nvfp4(x, amax_t=amax)
+            ops.gemm_nvfp4_seq2head(a, self._w_nvfp4, self._bias(x), recv_ptrs, rank, heads)
+            return
+        raise RuntimeError("QuantLinear has no quantised weights (call set_quant first)")
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """y = x @ W^T (+ bias) through the quantised GEMM; out dtype as the
         reference (x.dtype for bf16/fp16 input, else bf16)."""

@@ -6,8 +6,9 @@ non-CUDA tensors raise.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 
@@ -91,6 +92,18 @@ def gemm_i8(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor
     return out
 
 
+def gemm_i8_seq2head(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor,
+                     bias: Optional[torch.Tensor], recv_ptrs: Sequence[int], rank: int, heads: int) -> None:
+    """QKV GEMM whose output rows land in every head owner's receive buffer
+    [ws*m, 3, heads/ws, 128] (recv_ptrs in rank order): the seq->head
+    Ulysses exchange fused into the epilogue."""
+    _cuda(q, xs, w, ws, bias)
+    m, k = q.shape
+    arr = (ctypes.c_void_p * len(recv_ptrs))(*recv_ptrs)
+    call("h3b_gemm_i8_seq2head", q.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), _ptr(bias),
+         ctypes.cast(arr, ctypes.c_void_p), len(recv_ptrs), rank, heads, m, w.shape[0], k, _stream(q))
+
+
 def _gate_ld(gate: Optional[torch.Tensor]) -> int:
     if gate is None:
         return 0
@@ -161,6 +174,18 @@ def swap_nibbles(u8: torch.Tensor) -> torch.Tensor:
     dst = torch.empty_like(src)
     call("h3b_nvfp4_swap_nibbles", src.data_ptr(), dst.data_ptr(), src.numel(), _stream(src))
     return dst
+
+
+def gemm_nvfp4_seq2head(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor], recv_ptrs: Sequence[int],
+                        rank: int, heads: int) -> None:
+    """NVFP4 variant of gemm_i8_seq2head (both operands lo-first)."""
+    if a.hi_first or w.hi_first:
+        raise ValueError("gemm_nvfp4_seq2head needs tensor-core (lo-first) nibble order")
+    _cuda(a.codes, w.codes, bias)
+    arr = (ctypes.c_void_p * len(recv_ptrs))(*recv_ptrs)
+    call("h3b_gemm_nvfp4_seq2head", a.codes.data_ptr(), a.sf.data_ptr(), a.gs.data_ptr(), w.codes.data_ptr(),
+         w.sf.data_ptr(), w.gs.data_ptr(), _ptr(bias), ctypes.cast(arr, ctypes.c_void_p), len(recv_ptrs), rank,
+         heads, a.rows, w.rows, a.k, _stream(a.codes))
 
 
 def swiglu_interleave_perm(n: int, device=None) -> torch.Tensor:
@@ -244,6 +269,28 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optio
          heads, s_q,
          s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), out.stride(0), out.stride(1), scale, _stream(q))
     return out
+
+
+def attention_head2seq(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o_ptrs: Sequence[int], *,
+                       s_local: int, head0: int, total_heads: int, scale: Optional[float] = None,
+                       amax_out: Optional[torch.Tensor] = None) -> None:
+    """Attention over this rank's heads (q/k/v [S, H_local, 128] views of all
+    S tokens) writing query row t into rank t // s_local's out-projection
+    input [s_local, total_heads, 128] (o_ptrs[r]: device pointers valid in
+    this process, rank order) at head head0 + h — the head->sequence Ulysses
+    exchange fused into the epilogue."""
+    _cuda(q, k, v, amax_out)
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[-1] != 128 or t.stride(-1) != 1:
+            raise ValueError("attention expects bf16 [S, H, 128] views with unit last stride")
+    if k.stride() != v.stride():
+        raise ValueError("k and v must share strides")
+    s_q, heads, d = q.shape
+    scale = d ** -0.5 if scale is None else float(scale)
+    arr = (ctypes.c_void_p * len(o_ptrs))(*o_ptrs)
+    call("h3b_attention_fwd_head2seq", q.data_ptr(), k.data_ptr(), v.data_ptr(), ctypes.cast(arr, ctypes.c_void_p),
+         len(o_ptrs), s_local, head0, total_heads * d, d, _ptr(amax_out), heads, s_q, k.shape[0], q.stride(0),
+         q.stride(1), k.stride(0), k.stride(1), scale, _stream(q))
 
 
 def qk_rmsnorm_rope(q: torch.Tensor, k: Optional[torch.Tensor], q_weight: torch.Tensor,

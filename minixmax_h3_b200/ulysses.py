@@ -3,19 +3,102 @@
 Same contract as the reference's ops/ulysses.py:14-61: every rank holds
 S/ws tokens with all heads for the projections, and all S tokens with H/ws
 heads (rank r owns heads [r*H/ws, (r+1)*H/ws)) for attention; the sequence
-order after the exchange is the rank order.  The transport is NCCL
-``all_to_all_single`` over NVLink.  ``all_to_all_qkv`` moves the packed
-[S_local, 3, H, D] projection output in ONE exchange and returns q/k/v as
-strided views that the attention kernel reads in place.
+order after the exchange is the rank order.  Two transports:
+
+* ``nccl``: NCCL ``all_to_all_single`` over NVLink.  ``all_to_all_qkv``
+  moves the packed [S_local, 3, H, D] projection output in ONE exchange and
+  returns q/k/v as strided views that the attention kernel reads in place.
+* ``p2p`` (default with CUDA): no separate exchange.  The QKV GEMM epilogue
+  stores each output block straight into the head owner's receive buffer,
+  and the attention epilogue stores each output row into the token owner's
+  out-projection input, through buffers mapped by CUDA IPC
+  (``PeerBuffer``).  A collective on the compute stream orders each phase.
 """
 from __future__ import annotations
 
-from typing import Sequence
+import ctypes
+import os
+from typing import Optional, Sequence
 
 import torch
 import torch.distributed as tdist
 
+from ._lib import call
 from .dist import is_distributed, state
+
+
+def transport() -> str:
+    """"p2p" (fused P2P stores, default) or "nccl" (H3B_ULYSSES=nccl)."""
+    t = os.environ.get("H3B_ULYSSES", "p2p")
+    if t not in ("p2p", "nccl"):
+        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p or nccl")
+    return t
+
+
+class PeerBuffer:
+    """A device buffer allocated on every rank of the group, with every
+    peer's copy mapped into this process by CUDA IPC (ptrs[r] = rank r's
+    buffer, rank order).  Creation is collective (an all-gather of the IPC
+    handles), so every rank must create the same buffers in the same order."""
+
+    def __init__(self, shape: Sequence[int], dtype: torch.dtype, device: torch.device):
+        st = state()
+        self.local = torch.empty(tuple(shape), dtype=dtype, device=device)
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_int64()
+        call("h3b_ipc_export", self.local.data_ptr(), ctypes.cast(handle, ctypes.c_void_p), ctypes.byref(off))
+        rec = torch.tensor(list(bytes(handle)) + list(int(off.value).to_bytes(8, "little")), dtype=torch.uint8,
+                           device=device)
+        everyone = torch.empty(st.world_size * 72, dtype=torch.uint8, device=device)
+        tdist.all_gather_into_tensor(everyone, rec, group=st.group)
+        raw = bytes(everyone.cpu().tolist())
+        self.ptrs: list[int] = []
+        self._imported: list[tuple[int, int]] = []
+        for r in range(st.world_size):
+            if r == st.rank:
+                self.ptrs.append(self.local.data_ptr())
+                continue
+            h = (ctypes.c_uint8 * 64).from_buffer_copy(raw[72 * r:72 * r + 64])
+            o = int.from_bytes(raw[72 * r + 64:72 * r + 72], "little")
+            p = ctypes.c_void_p()
+            call("h3b_ipc_import", ctypes.cast(h, ctypes.c_void_p), o, ctypes.byref(p))
+            self.ptrs.append(int(p.value))
+            self._imported.append((int(p.value), o))
+
+    def close(self) -> None:
+        for p, o in self._imported:
+            call("h3b_ipc_close", p, o)
+        self._imported.clear()
+
+
+_PEER_BUFS: dict[tuple, PeerBuffer] = {}
+
+
+def peer_buffer(name: str, shape: Sequence[int], dtype: torch.dtype, device: torch.device) -> PeerBuffer:
+    """Cached PeerBuffer per (name, shape, dtype, device), reused across
+    blocks and steps like the reference's SP buffers (runtime/dist.py:172-203)."""
+    key = (name, tuple(shape), dtype, str(device))
+    buf = _PEER_BUFS.get(key)
+    if buf is None:
+        buf = _PEER_BUFS[key] = PeerBuffer(shape, dtype, device)
+    return buf
+
+
+def release_peer_buffers() -> None:
+    """Unmaps every peer buffer (call before destroying the process group)."""
+    for buf in _PEER_BUFS.values():
+        buf.close()
+    _PEER_BUFS.clear()
+
+
+def phase_barrier(device: torch.device, flag: Optional[torch.Tensor] = None) -> None:
+    """Orders a P2P exchange: a collective on the compute stream completes on
+    a rank only after every rank's preceding launches (the P2P stores into
+    this rank's buffers) have completed.  `flag` (fp32 [1]) is max-reduced
+    and can carry a value the step needs anyway (an amax)."""
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.float32, device=device)
+    tdist.all_reduce(flag, op=tdist.ReduceOp.MAX, group=state().group)
 
 
 def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:

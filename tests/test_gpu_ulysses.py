@@ -1,7 +1,9 @@
 """Multi-GPU parity of the Ulysses DiT block (needs >= 2 GPUs; skipped otherwise).
 
-Two NCCL ranks each run their sequence shard of one DiT block; the gathered
-result must match the same block run on one GPU.  With INT8 (per-token
+Two NCCL ranks each run their sequence shard of one DiT block, with the
+exchanges either fused into the kernels as P2P stores (transport "p2p") or
+as NCCL all-to-alls ("nccl"); the gathered result must match the same block
+run on one GPU.  With INT8 (per-token
 activation scales) every token sees identical arithmetic on both paths, so the
 match is exact.  With NVFP4 the activation global scales are max-reduced
 across ranks (block.global_amax_), so the sharded run quantises exactly as
@@ -27,10 +29,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, ws: int, port: int, fmt: str, out_q) -> None:
+def _worker(rank: int, ws: int, port: int, fmt: str, transport: str, mlp_act: str, out_q) -> None:
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(ws),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), H3B_ULYSSES=transport)
     import torch.distributed as tdist
 
     from minixmax_h3_b200 import dist as hdist
@@ -42,7 +44,7 @@ def _worker(rank: int, ws: int, port: int, fmt: str, out_q) -> None:
         dev = torch.device("cuda", rank)
         hidden, heads = 512, 4
         blk = DiTBlock(hidden, heads, 128, 4 * hidden, 256, 1e-6, 1e-6, dtype=torch.bfloat16, device=dev,
-                       mlp_act="gelu")
+                       mlp_act=mlp_act)
         init_block_random(blk, fmt, torch.Generator(device=dev).manual_seed(0))  # same on every rank
         pos = RopeSpec.grid_positions(4, 16, 24)
         rope = RopeSpec.build(pos, device=dev)
@@ -72,14 +74,20 @@ def _worker(rank: int, ws: int, port: int, fmt: str, out_q) -> None:
         raise
 
 
-@pytest.mark.parametrize("fmt", ["int8_tensorwise", "nvfp4"])
-def test_ulysses_block_matches_single_gpu(fmt):
+@pytest.mark.parametrize("fmt,transport,mlp_act", [
+    ("int8_tensorwise", "p2p", "gelu"),
+    ("nvfp4", "p2p", "gelu"),
+    ("nvfp4", "p2p", "swiglu"),
+    ("int8_tensorwise", "nccl", "gelu"),
+    ("nvfp4", "nccl", "gelu"),
+])
+def test_ulysses_block_matches_single_gpu(fmt, transport, mlp_act):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, fmt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, fmt, transport, mlp_act, q)) for r in range(2)]
     for p in procs:
         p.start()
     try:
