@@ -278,19 +278,48 @@ H3B_DEV float e4m3_to_f32(uint32_t b) {
   return __uint_as_float(((e + 120u) << 23) | (mnt << 20));  // (1 + mnt/8) * 2^(e-7)
 }
 
-// e2m1 magnitude code of |a| with round-half-even and saturation at 6.
-H3B_DEV uint32_t e2m1_mag(float a) {
-  if (a <= 0.25f) return 0u;
-  if (a < 0.75f) return 1u;
-  if (a <= 1.25f) return 2u;
-  if (a < 1.75f) return 3u;
-  if (a <= 2.5f) return 4u;
-  if (a < 3.5f) return 5u;
-  if (a <= 5.0f) return 6u;
-  return 7u;
+H3B_DEV float nvfp4_global_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f; }
+
+// RN(a / b) from y = RN(1/b) by Markstein's correction: q0 = RN(a*y) is within
+// one ulp of a/b, the FMA residual a - q0*b is exact, and RN(q0 + r*y) is the
+// correctly rounded quotient (Markstein 1990) — three FMA-pipe operations
+// instead of a full division per element.  The theorem needs no overflow or
+// underflow in the residual; callers take __fdiv_rn outside
+// |a| >= 2^-90 and 2^-96 <= b <= 2^96.
+H3B_DEV float div_rn_by_rcp(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, y, q0);
 }
 
-H3B_DEV float nvfp4_global_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f; }
+H3B_DEV bool rcp_div_ok(float b) { return b >= 0x1p-96f && b <= 0x1p96f; }
+
+// Four packed e2m1 bytes of r[0..7] with the hardware's round-half-even,
+// saturate-at-6 conversion (the recipe's e2m1_rne_sat; the sign of zero is
+// kept).  hi_first: element 2i in the high nibble of byte i.
+H3B_DEV uint32_t e2m1x8(const float* r, int hi_first) {
+  uint32_t out;
+  if (hi_first) {
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %1, %2;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %3, %4;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %5, %6;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %7, %8;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(out)
+        : "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]), "f"(r[6]), "f"(r[7]));
+  } else {
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(out)
+        : "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]), "f"(r[6]), "f"(r[7]));
+  }
+  return out;
+}
 
 __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int64_t m,
                                                           int64_t k, int64_t ldx, int64_t rows_padded,
@@ -312,6 +341,8 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
   }
   const __nv_bfloat16* xr = x + row * ldx + g * 64;
   const float six_gs = 6.0f * gs;
+  const bool six_ok = rcp_div_ok(six_gs);
+  const float y6 = __frcp_rn(six_gs);
   uint32_t sf_word = 0u;
   uint32_t out_words[8];
 #pragma unroll
@@ -332,30 +363,25 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
     float amax_b = 0.0f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) amax_b = fmaxf(amax_b, fabsf(f[j]));
-    const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(__fdiv_rn(amax_b, six_gs), __NV_SATFINITE, __NV_E4M3);
+    const float ratio = (six_ok && amax_b >= 0x1p-90f) ? div_rn_by_rcp(amax_b, six_gs, y6) : __fdiv_rn(amax_b, six_gs);
+    const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(ratio, __NV_SATFINITE, __NV_E4M3);
     const uint32_t sbits = static_cast<uint32_t>(sb) & 0xFFu;
     sf_word |= sbits << (8 * b);
     const float sval = e4m3_to_f32(sbits);
     const float denom = sval * gs;
-    uint32_t w0 = 0u, w1 = 0u;
+    float r[16];
+    if (sval > 0.0f) {
+      const bool ok = rcp_div_ok(denom);
+      const float y = __frcp_rn(denom);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      uint32_t code = 0u;
-      if (sval > 0.0f) {
-        const float r = __fdiv_rn(f[j], denom);
-        code = e2m1_mag(fabsf(r)) | (signbit(r) ? 8u : 0u);
-      }
-      const int byte = j >> 1;
-      const bool even = (j & 1) == 0;
-      const uint32_t shift = (even == (hi_first != 0)) ? 4u : 0u;
-      const uint32_t val = code << (shift + 8u * (byte & 3));
-      if (byte < 4)
-        w0 |= val;
-      else
-        w1 |= val;
+      for (int j = 0; j < 16; ++j)
+        r[j] = (ok && fabsf(f[j]) >= 0x1p-90f) ? div_rn_by_rcp(f[j], denom, y) : __fdiv_rn(f[j], denom);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = 0.0f;  // an all-zero block: every code is +0
     }
-    out_words[2 * b] = w0;
-    out_words[2 * b + 1] = w1;
+    out_words[2 * b] = e2m1x8(r, hi_first);
+    out_words[2 * b + 1] = e2m1x8(r + 8, hi_first);
   }
   uint8_t* cr = codes + row * (k >> 1) + g * 32;
   *reinterpret_cast<uint4*>(cr) = make_uint4(out_words[0], out_words[1], out_words[2], out_words[3]);

@@ -86,6 +86,32 @@ def test_nvfp4_bit_exact(cuda, m, k):
     assert torch.equal(got.sf.cpu(), want["sf"])
 
 
+@pytest.mark.parametrize("scale", [1.0, 1e-30, 1e25])
+@pytest.mark.parametrize("hi_first", [True, False])
+def test_nvfp4_wide_range_bit_exact(cuda, scale, hi_first):
+    """Magnitudes spread over 2^-40 .. 2^40 within the tensor (blocks far
+    below the global max, signed zeros, exact ties), at three overall
+    scales, so the reciprocal-based division, its range guards and the
+    exact-division fallback are all exercised."""
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(int(abs(torch.tensor(scale).log10())) + hi_first)
+    m, k = 512, 1024
+    mant = 1.0 + torch.rand(m, k, generator=g)
+    expo = torch.randint(-40, 41, (m, k), generator=g).float()
+    sign = torch.where(torch.rand(m, k, generator=g) < 0.5, -1.0, 1.0)
+    x = sign * mant * torch.exp2(expo) * scale
+    x[3] = 0.0
+    x[4] = -0.0
+    x[5, :64] = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0] * 8) * scale  # e2m1 ties
+    x = x.to(torch.bfloat16)
+    got = ops.quant_nvfp4(x.to(cuda), hi_first=hi_first)
+    want = O.nvfp4_quantize(x, hi_first=hi_first)
+    assert torch.equal(got.gs.cpu(), want["gs"])
+    assert torch.equal(got.sf.cpu(), want["sf"])
+    assert torch.equal(got.codes.cpu(), want["codes"])
+
+
 def test_amax_and_zero_input(cuda):
     from minixmax_h3_b200 import ops
 
