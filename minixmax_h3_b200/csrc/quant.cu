@@ -60,6 +60,20 @@ H3B_DEV float block_max(float v, float* red) {
   return red[32];
 }
 
+// RN(a / b) from y = RN(1/b) by Markstein's correction: q0 = RN(a*y) is within
+// one ulp of a/b, the FMA residual a - q0*b is exact, and RN(q0 + r*y) is the
+// correctly rounded quotient (Markstein 1990) — three FMA-pipe operations
+// instead of a full division per element.  The theorem needs no overflow or
+// underflow in the residual; callers take __fdiv_rn outside
+// |a| >= 2^-90 and 2^-96 <= b <= 2^96.
+H3B_DEV float div_rn_by_rcp(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, y, q0);
+}
+
+H3B_DEV bool rcp_div_ok(float b) { return b >= 0x1p-96f && b <= 0x1p96f; }
+
 template <typename T, int THREADS, int MAXV>
 __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restrict__ x, int64_t k, int64_t ldx,
                                                                 int8_t* __restrict__ q, float* __restrict__ scale) {
@@ -83,6 +97,8 @@ __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restr
   amax = block_max<THREADS>(amax, red);
   amax = fmaxf(amax, 1e-12f);
   const float s = __fdiv_rn(amax, 127.0f);
+  const bool fast = rcp_div_ok(s);
+  const float y = __frcp_rn(s);
   int8_t* qr = q + row * k;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
@@ -93,7 +109,7 @@ __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restr
       uint32_t packed[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float r = rintf(__fdiv_rn(f[j], s));
+        float r = rintf((fast && fabsf(f[j]) >= 0x1p-90f) ? div_rn_by_rcp(f[j], s, y) : __fdiv_rn(f[j], s));
         r = fminf(fmaxf(r, -128.0f), 127.0f);
         const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
         packed[j >> 2] |= b << ((j & 3) * 8);
@@ -220,6 +236,8 @@ __global__ void __launch_bounds__(256) quant_i8_rows_rot_kernel(const T* __restr
   amax = block_max<256>(amax, red);
   amax = fmaxf(amax, 1e-12f);
   const float s = __fdiv_rn(amax, 127.0f);
+  const bool fast = rcp_div_ok(s);
+  const float y = __frcp_rn(s);
   int8_t* qr = q + row * k;
 #pragma unroll
   for (int i = 0; i < MAXG; ++i) {
@@ -228,7 +246,8 @@ __global__ void __launch_bounds__(256) quant_i8_rows_rot_kernel(const T* __restr
       uint32_t packed[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float r = rintf(__fdiv_rn(f[i][j], s));
+        const float fj = f[i][j];
+        float r = rintf((fast && fabsf(fj) >= 0x1p-90f) ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
         r = fminf(fmaxf(r, -128.0f), 127.0f);
         const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
         packed[j >> 2] |= b << ((j & 3) * 8);
@@ -279,20 +298,6 @@ H3B_DEV float e4m3_to_f32(uint32_t b) {
 }
 
 H3B_DEV float nvfp4_global_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f; }
-
-// RN(a / b) from y = RN(1/b) by Markstein's correction: q0 = RN(a*y) is within
-// one ulp of a/b, the FMA residual a - q0*b is exact, and RN(q0 + r*y) is the
-// correctly rounded quotient (Markstein 1990) — three FMA-pipe operations
-// instead of a full division per element.  The theorem needs no overflow or
-// underflow in the residual; callers take __fdiv_rn outside
-// |a| >= 2^-90 and 2^-96 <= b <= 2^96.
-H3B_DEV float div_rn_by_rcp(float a, float b, float y) {
-  const float q0 = __fmul_rn(a, y);
-  const float r = __fmaf_rn(-q0, b, a);
-  return __fmaf_rn(r, y, q0);
-}
-
-H3B_DEV bool rcp_div_ok(float b) { return b >= 0x1p-96f && b <= 0x1p96f; }
 
 // Four packed e2m1 bytes of r[0..7] with the hardware's round-half-even,
 // saturate-at-6 conversion (the recipe's e2m1_rne_sat; the sign of zero is
