@@ -7,14 +7,21 @@
 //                  ue4m3 scale per 16 elements copied smem -> TMEM with
 //                  tcgen05.cp, epilogue y = acc * a_gs * w_gs (+ bias[n]).
 //
-// Structure (one CTA per SM, persistent over 128 x BN output tiles):
-//   warp 0      TMA producer: A tile 128x128B, B tile BNx128B (+ scale
-//               factors by plain bulk copies) into a 4-deep smem ring.
-//   warp 1      TMEM allocator and single-thread MMA issuer; tcgen05.commit
-//               releases smem slots and publishes finished accumulators.
-//   warps 2-5   epilogue: tcgen05.ld 32x32b (one output row per thread),
-//               fp32 dequant/bias/activation/gate-residual, bf16 rows staged
-//               in 64B-swizzled shared memory and written by TMA stores.
+// Structure (persistent, one CTA per SM; for M > 128 the CTAs work in
+// clusters of two on 256 x BN tiles with cta_group::2 MMAs):
+//   warp 0      TMA producer: this CTA's 128 rows of A, its BN/PAIR rows of B
+//               (+ scale factors) into a 4- or 6-deep smem ring.  In a pair,
+//               both CTAs' copies complete on the leader's full barrier,
+//               which only the leader arms (for both CTAs' bytes).
+//   warp 1      TMEM allocator; in the leader (the only CTA of a single-CTA
+//               launch) the single-thread MMA issuer.  tcgen05.commit (to
+//               both CTAs of a pair) releases smem slots and publishes
+//               finished accumulators.
+//   warps 2-5   epilogue of this CTA's 128 accumulator rows: tcgen05.ld
+//               32x32b (one output row per thread), fp32 dequant/bias and
+//               GELU / SwiGLU / gate-residual / seq->head scatter, bf16
+//               blocks staged in 64B-swizzled shared memory and written by
+//               TMA stores; each warp releases the accumulator to the leader.
 // Accumulators are double-buffered in TMEM (columns 0 and 256), so the MMAs
 // of tile t+1 run while the epilogue drains tile t:
 //   INT8:  BN = 256.
@@ -23,17 +30,11 @@
 //          behind the MMAs that read it.  A 192-row N tile starts either
 //          on a 128-row scale block (even tiles) or 64 rows into one (odd
 //          tiles): the two blocks covering it are copied and the MMA's SFB
-//          address skips 2 TMEM columns (= 64 rows) for odd tiles.
+//          address skips 2 TMEM columns (= 64 rows) for odd tiles.  In a
+//          pair each CTA copies its own A scales and the tile's B scales.
 // Operands are K-major with the 128-byte swizzle.  No load uses cluster
-// multicast.  Every wait is bounded.
-//
-// Sequence->head scatter (the Ulysses exchange fused into the QKV
-// projection, ops/ulysses.py:14-30 after model/dit.py:169-190): each 32x32
-// output block lies in one (q|k|v, head) slice and is TMA-stored straight
-// into the receive buffer [ws*m, 3, H/ws, 128] of the rank that owns the
-// head, at this rank's rows, through one tensor map per destination whose
-// rows are clipped to this rank's range.  Destinations are this GPU's own
-// buffer or peers' buffers mapped by CUDA IPC (plain stores over NVLink).
+// multicast.  Every wait is bounded; both CTAs of a pair stay resident until
+// a final cluster barrier.
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
 
@@ -42,8 +43,8 @@ H3B_REGISTER_STATUS_READER(gemm);
 
 namespace {
 
-constexpr int BM = 128;
-constexpr int STAGES = 4;
+constexpr int BM = 128;       // accumulator rows per CTA (TMEM lanes)
+constexpr int MAX_STAGES = 6;
 constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
 constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
 constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
@@ -82,16 +83,24 @@ struct GemmArgs {
   int hd;              // OUT_SEQ2HEAD: H * 128 (columns per q|k|v part)
 };
 
-template <int KIND>
+// PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per
+// 256 x BN tile with cta_group::2 MMAs issued by the leader (rank 0): each
+// CTA stages its 128 rows of A and BN/2 rows of B, and holds its 128 rows of
+// the accumulator, so each SM moves half as much B through shared memory.
+template <int KIND, int PAIR>
 struct Cfg {
-  static constexpr int BN = KIND == KIND_I8 ? 256 : 192;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int BN = KIND == KIND_I8 ? 256 : 192;  // MMA N
+  static constexpr int B_ROWS = BN / PAIR;                 // B rows staged by this CTA
+  static constexpr int B_BYTES = B_ROWS * 128;
+  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
   static constexpr int SF_COLS_PER_SLOT = 48;  // 16 (A) + 32 (B)
   static constexpr int TMEM_COLS = 512;
   static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
+  static constexpr int TX_BYTES = PAIR * STAGE_BYTES;  // the leader's full barrier counts both CTAs' bytes
   static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
-  static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM, BN) : idesc_nvf4(BM, BN);
+  static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM * PAIR, BN) : idesc_nvf4(BM * PAIR, BN);
+  static_assert(STAGES <= MAX_STAGES, "barrier arrays");
   static_assert(BN <= ACC_STRIDE, "accumulator overlap");
   static_assert(KIND == KIND_I8 || BN + SF_COLS_PER_SLOT <= ACC_STRIDE, "SF slot overlaps an accumulator");
   static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
@@ -101,8 +110,8 @@ struct Cfg {
 H3B_DEV uint32_t sf_slot_col(int slot) { return 192u + static_cast<uint32_t>(slot) * ACC_STRIDE; }
 
 struct __align__(8) Barriers {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -111,11 +120,14 @@ struct __align__(8) Barriers {
   int consumed;  // k-slabs whose full barrier the MMA thread has observed
 };
 
-template <int KIND>
+template <int KIND, int PAIR>
 constexpr size_t smem_bytes() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * Cfg<KIND>::STAGE_BYTES +
+  return 1024 /*alignment slack*/ + static_cast<size_t>(Cfg<KIND, PAIR>::STAGES) * Cfg<KIND, PAIR>::STAGE_BYTES +
          4 * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
 }
+static_assert(smem_bytes<KIND_NVF4, 2>() <= 227 * 1024 && smem_bytes<KIND_I8, 2>() <= 227 * 1024 &&
+                  smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 && smem_bytes<KIND_I8, 1>() <= 227 * 1024,
+              "shared memory budget");
 
 H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
@@ -131,13 +143,15 @@ H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* a
 // buffer must be 512-byte aligned.
 H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
-template <int KIND>
+template <int KIND, int PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ PeerMaps peers,
+                const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                 const GemmArgs args) {
-  using C = Cfg<KIND>;
+  using C = Cfg<KIND, PAIR>;
   constexpr int BN = C::BN;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -149,7 +163,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tiles = (args.m + BM - 1) / BM;
+  const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0u;  // CTA within the pair; 0 = leader
+  const bool leader = rank == 0;
+  const int cluster = static_cast<int>(blockIdx.x) / PAIR, n_clusters = static_cast<int>(gridDim.x) / PAIR;
+  const int m_tiles = (args.m + BM * PAIR - 1) / (BM * PAIR);
   const int n_tiles = (args.n + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int nk = args.k / C::K_PER_STAGE;
@@ -162,7 +179,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      mbar_init(&bars->acc_empty[b], EPI_THREADS);
+      mbar_init(&bars->acc_empty[b], 4 * PAIR);  // one arrival per epilogue warp of each CTA
     }
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
@@ -173,11 +190,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tmap_y);
   }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR == 2) {
+      tmem_alloc_pair(&bars->tmem_base, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR == 2) {
+    cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
@@ -186,9 +212,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
         const int mt = tile / n_tiles, nt = tile % n_tiles;
-        const int m0 = mt * BM;
+        const int m0 = (mt * PAIR + static_cast<int>(rank)) * BM;  // this CTA's A rows
         const int n0 = nt * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
@@ -196,6 +222,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1, &g_status, 1, abort_flag)) {
             ok = false;
             break;
+          }
+          if constexpr (PAIR == 2) {
+            // Both CTAs' copies complete on the leader's full[s]; only the
+            // leader arms it, for the pair's bytes.
+            const uint32_t full_l = mapa_shared(smem_u32(&bars->full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&bars->full[s], C::TX_BYTES);
+            tma_load_2d_pair(sA + s * A_BYTES, &tmap_a, kb * 128, m0, full_l);
+            tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, kb * 128, n0 + static_cast<int>(rank) * C::B_ROWS,
+                             full_l);
+            if constexpr (KIND == KIND_NVF4) {
+              // Scale rows of 512 bytes (one 128-row block x 4 scale columns):
+              // A: this CTA's block, B: the tile's two 128-row blocks.
+              const int ncb = args.k / 64;
+              const int nb0 = n0 / 128;
+              const int nb1 = (nb0 + 1) * 128 < args.n ? nb0 + 1 : nb0;
+              tma_load_2d_pair(sSFA + s * SFA_BYTES, &tmap_sfa, 0, (m0 / 128) * ncb + kb * 4, full_l);
+              tma_load_2d_pair(sSFB + s * SFB_BYTES, &tmap_sfb, 0, nb0 * ncb + kb * 4, full_l);
+              tma_load_2d_pair(sSFB + s * SFB_BYTES + SFB_BYTES / 2, &tmap_sfb, 0, nb1 * ncb + kb * 4, full_l);
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
           tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * 128, m0, &bars->full[s]);
@@ -217,21 +263,31 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok || *abort_flag) {
-        // Drain: wait (bounded) for every slab issued but not yet consumed, so
-        // no bulk copy is still writing this CTA's shared memory at exit.
-        const int consumed = *reinterpret_cast<volatile int*>(&bars->consumed);
-        for (int j = consumed; j < it; ++j) {
-          mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+        if (leader) {
+          // Drain: wait (bounded) for every slab issued but not yet consumed,
+          // so no copy is still writing this CTA's shared memory at exit.
+          const int consumed = *reinterpret_cast<volatile int*>(&bars->consumed);
+          for (int j = consumed; j < it; ++j) {
+            mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+          }
+        } else {
+          // The peer's copies complete on the leader's barriers, which it
+          // cannot wait on: give its copies in flight a bounded 200 us to
+          // land (both CTAs stay resident until the final cluster barrier).
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (the leader only under PAIR = 2: its MMAs fill both CTAs' TMEM)
+    if (lane == 0 && leader) {
       int it = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters, ++local) {
         const int buf = local & 1;
         const int use = local >> 1;
         if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
@@ -255,7 +311,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           if constexpr (KIND == KIND_I8) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
+              if constexpr (PAIR == 2)
+                mma_i8_ss_pair(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
+              else
+                mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
             }
           } else {
             // tcgen05.cp and tcgen05.mma issued by this one thread execute in
@@ -263,27 +322,45 @@ __global__ void __launch_bounds__(THREADS, 1)
             // overtake the MMAs of slab it-2 that read it (the pattern
             // CUTLASS's block-scaled mainloop relies on with a single slot).
             const uint32_t sf_col = tmem_base + sf_slot_col(it & 1);
+            auto cp = [&](uint32_t taddr, uint64_t desc) {
+              if constexpr (PAIR == 2)
+                tc_cp_32x128b_x4_pair(taddr, desc);  // each CTA: its own scales -> its own TMEM
+              else
+                tc_cp_32x128b_x4(taddr, desc);
+            };
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              tc_cp_32x128b_x4(sf_col + j * 4, sdesc_plain_rows16(smem_u32(sSFA + s * SFA_BYTES + j * 512)));
-              tc_cp_32x128b_x4(sf_col + 16 + j * 8,
-                               sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + j * 512)));
-              tc_cp_32x128b_x4(sf_col + 16 + j * 8 + 4,
-                               sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + SFB_BYTES / 2 + j * 512)));
+              cp(sf_col + j * 4, sdesc_plain_rows16(smem_u32(sSFA + s * SFA_BYTES + j * 512)));
+              cp(sf_col + 16 + j * 8, sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + j * 512)));
+              cp(sf_col + 16 + j * 8 + 4, sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + SFB_BYTES / 2 + j * 512)));
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
-                          sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
+              if constexpr (PAIR == 2)
+                mma_nvf4_ss_pair(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
+                                 sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
+              else
+                mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
+                            sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
             }
           }
-          tc_commit(&bars->empty[s]);  // slot reusable once these MMAs have read it
+          // slot reusable (in both CTAs) once these MMAs have read it
+          if constexpr (PAIR == 2)
+            tc_commit_pair_mc(&bars->empty[s], 0x3);
+          else
+            tc_commit(&bars->empty[s]);
         }
         if (!ok) break;
-        tc_commit(&bars->acc_full[buf]);  // accumulator complete
+        if constexpr (PAIR == 2)  // accumulator complete in both CTAs
+          tc_commit_pair_mc(&bars->acc_full[buf], 0x3);
+        else
+          tc_commit(&bars->acc_full[buf]);
       }
       // Drain all MMAs this thread issued before TMEM is released.
-      tc_commit(&bars->drain);
+      if constexpr (PAIR == 2)
+        tc_commit_pair(&bars->drain);
+      else
+        tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
     }
   } else {
@@ -294,12 +371,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
     int stage_seq = 0;                      // alternates this warp's two staging buffers
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    // acc_empty lives in the leader; the peer's warps arrive remotely.
+    auto release_acc = [&](int buf) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR == 2)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&bars->acc_empty[buf]), 0));
+        else
+          mbar_arrive(&bars->acc_empty[buf]);
+      }
+    };
+    for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
       const int buf = local & 1;
       const int use = local >> 1;
       if (!warp_wait(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
       tc_fence_after();
-      const int m0 = (tile / n_tiles) * BM;
+      const int m0 = ((tile / n_tiles) * PAIR + static_cast<int>(rank)) * BM;
       const int n0 = (tile % n_tiles) * BN;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.m;
@@ -372,10 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_wait_ld();
           reg_fence32(rg);
           reg_fence32(ru);
-          if (p == BN / 64 - 1) {
-            tc_fence_before();
-            mbar_arrive(&bars->acc_empty[buf]);
-          }
+          if (p == BN / 64 - 1) release_acc(buf);
           const int gcol = n0 + p * 64;
           if (gcol >= args.n) continue;  // warp-uniform
           float v[32];
@@ -394,10 +479,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32p(t_row + c * 32, r);
         tmem_wait_fence<1>(r);
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&bars->acc_empty[buf]);
-        }
+        if (c == BN / 32 - 1) release_acc(buf);
         const int col0 = n0 + c * 32;
         if (col0 >= args.n) continue;  // warp-uniform: the whole chunk is past the last column
         if (args.out_mode == OUT_I32) {
@@ -446,22 +528,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR == 2) {
+    cluster_sync();  // neither CTA leaves while its partner may still signal it
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR == 2)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
-template <int KIND>
-int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
-                cudaStream_t st, const PeerMaps* peer_maps = nullptr) {
-  using C = Cfg<KIND>;
-  CUtensorMap ta, tb, ty;
+template <int KIND, int PAIR>
+int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
+                  cudaStream_t st, const PeerMaps* peer_maps) {
+  using C = Cfg<KIND, PAIR>;
+  CUtensorMap ta, tb, ty, tsfa, tsfb;
   int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
-  rc = h3b::encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, b_row_bytes, args.n, b_row_bytes, 128, C::BN,
+  rc = h3b::encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, b_row_bytes, args.n, b_row_bytes, 128, C::B_ROWS,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
   if (args.out_mode == OUT_BF16) {
@@ -473,21 +562,62 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
   } else {
     ty = ta;  // the int32 and scatter paths never use this map
   }
-  const size_t smem = smem_bytes<KIND>();
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[KIND]) {
-    if (cudaFuncSetAttribute(gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  tsfa = ta;
+  tsfb = ta;
+  if (KIND == KIND_NVF4 && PAIR == 2) {
+    // Blocked scales as rows of 512 bytes (64 x u64): one 128-row block x 4
+    // scale columns per row; a K slab's scales are 4 consecutive rows.
+    const int64_t ncb = args.k / 64;
+    rc = h3b::encode_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT64, args.a_sf, 64, (args.m + 127) / 128 * ncb, 512, 64,
+                        4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != H3B_OK) return rc;
+    rc = h3b::encode_2d(&tsfb, CU_TENSOR_MAP_DATA_TYPE_UINT64, args.w_sf, 64, (args.n + 127) / 128 * ncb, 512, 64,
+                        4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != H3B_OK) return rc;
+  }
+  const size_t smem = smem_bytes<KIND, PAIR>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_kernel<KIND, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return H3B_ERR_LAUNCH;
-    attr_set[KIND] = true;
+    attr_set = true;
   }
-  const int m_tiles = static_cast<int>((args.m + BM - 1) / BM);
+  const int m_tiles = static_cast<int>((args.m + BM * PAIR - 1) / (BM * PAIR));
   const int n_tiles = static_cast<int>((args.n + C::BN - 1) / C::BN);
   const int tiles = m_tiles * n_tiles;
-  const int grid = tiles < h3b::num_sms() ? tiles : h3b::num_sms();
+  const int max_units = h3b::num_sms() / PAIR;
+  const int units = tiles < max_units ? tiles : max_units;
   static const PeerMaps no_peers = {};
-  gemm_kernel<KIND><<<grid, THREADS, smem, st>>>(ta, tb, ty, peer_maps ? *peer_maps : no_peers, args);
+  const PeerMaps& pm = peer_maps ? *peer_maps : no_peers;
+  if constexpr (PAIR == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * units));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, 2>, ta, tb, ty, pm, tsfa, tsfb, args) != cudaSuccess)
+      return H3B_ERR_LAUNCH;
+  } else {
+    gemm_kernel<KIND, 1><<<units, THREADS, smem, st>>>(ta, tb, ty, pm, tsfa, tsfb, args);
+  }
   return h3b::launch_status();
+}
+
+// CTA pairs for every GEMM with more than one 128-row tile of M; a single
+// row tile keeps one CTA per output tile (twice the CTAs for small M).
+template <int KIND>
+int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
+                cudaStream_t st, const PeerMaps* peer_maps = nullptr) {
+  if (args.m > BM) return launch_gemm_t<KIND, 2>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  return launch_gemm_t<KIND, 1>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
 }
 
 int check_common(int64_t m, int64_t n, int64_t k, int64_t kmul) {
