@@ -30,8 +30,8 @@ from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
-from .ulysses import (all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer, phase_barrier,
-                      split_range, transport)
+from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer,
+                      phase_barrier, split_range, transport)
 
 
 @dataclass
@@ -160,6 +160,7 @@ class Attention(nn.Module):
         sp = self.sequence_parallel and is_distributed()
         if sp and transport() == "p2p":
             return self._forward_p2p(h, rope_freqs, amax_h=amax_h, resid=resid, gate=gate, row_sel=row_sel)
+        gather_kv = sp and transport() == "allgather"
         qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
         if rope_freqs is not None:
@@ -174,7 +175,16 @@ class Attention(nn.Module):
             ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
                                 pos0, 0, zeros, 64, 0)
         amax_o = torch.zeros(1, dtype=torch.float32, device=h.device)
-        if sp:
+        if gather_kv:
+            # the reference's production SP (model/dit.py:200-248): local
+            # queries over the gathered keys/values of all ranks, all heads
+            k, v = all_gather_kv(q3[:, 1], q3[:, 2])
+            flops = 4.0 * s_local * k.shape[0] * self.head_dim * self.heads
+            o = ATTN_TIMER.record(lambda: ops.attention(q3[:, 0], k, v, scale=self.head_dim ** -0.5,
+                                                        amax_out=amax_o), flops)
+            o = o.view(s_local, self.heads * self.head_dim)
+            global_amax_(amax_o, self.out_proj)
+        elif sp:
             q, k, v = all_to_all_qkv(qkv, self.heads, self.head_dim)
             flops = 4.0 * q.shape[0] * k.shape[0] * self.head_dim * q.shape[1]
             o = ATTN_TIMER.record(lambda: ops.attention(q, k, v, scale=self.head_dim ** -0.5), flops)
@@ -191,7 +201,6 @@ class Attention(nn.Module):
             return self.out_proj.forward_fused(o, amax=amax_o, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
                                                row_sel=row_sel)
         return self.out_proj.forward_fused(o, amax=amax_o)
-
 
     def _forward_p2p(self, h: torch.Tensor, rope_freqs: Optional[RopeSpec], *, amax_h=None, resid=None,
                      gate=None, row_sel=None) -> torch.Tensor:

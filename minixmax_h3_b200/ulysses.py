@@ -3,7 +3,8 @@
 Same contract as the reference's ops/ulysses.py:14-61: every rank holds
 S/ws tokens with all heads for the projections, and all S tokens with H/ws
 heads (rank r owns heads [r*H/ws, (r+1)*H/ws)) for attention; the sequence
-order after the exchange is the rank order.  Two transports:
+order after the exchange is the rank order.  Three sequence-parallel
+schemes (``H3B_ULYSSES``):
 
 * ``nccl``: NCCL ``all_to_all_single`` over NVLink.  ``all_to_all_qkv``
   moves the packed [S_local, 3, H, D] projection output in ONE exchange and
@@ -13,6 +14,10 @@ order after the exchange is the rank order.  Two transports:
   and the attention epilogue stores each output row into the token owner's
   out-projection input, through buffers mapped by CUDA IPC
   (``PeerBuffer``).  A collective on the compute stream orders each phase.
+* ``allgather``: the reference's production scheme (model/dit.py:200-248):
+  no head exchange; K and V of all tokens are gathered once
+  (``all_gather_kv``, runtime/dist.py:291-312) and every rank attends its
+  own queries over all keys, all heads.
 """
 from __future__ import annotations
 
@@ -28,10 +33,10 @@ from .dist import is_distributed, state
 
 
 def transport() -> str:
-    """"p2p" (fused P2P stores, default) or "nccl" (H3B_ULYSSES=nccl)."""
+    """"p2p" (fused P2P stores, default), "nccl" or "allgather" (H3B_ULYSSES)."""
     t = os.environ.get("H3B_ULYSSES", "p2p")
-    if t not in ("p2p", "nccl"):
-        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p or nccl")
+    if t not in ("p2p", "nccl", "allgather"):
+        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p, nccl or allgather")
     return t
 
 
@@ -147,6 +152,19 @@ def all_to_all_qkv(qkv: torch.Tensor, heads: int, head_dim: int
     tdist.all_to_all_single(recv, send, group=state().group)
     r = recv.view(ws * s_local, 3, hl, head_dim)
     return r[:, 0], r[:, 1], r[:, 2]
+
+
+def all_gather_kv(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[S_local, H, D] k and v of every rank -> [S, H, D] views of one gathered
+    buffer, rank order = sequence order (runtime/dist.py:291-312 with
+    seq_dim=0: one collective for K and V together)."""
+    if not is_distributed():
+        return k, v
+    st = state()
+    kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
+    out = torch.empty((st.world_size * kv.shape[0],) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
+    tdist.all_gather_into_tensor(out, kv, group=st.group)
+    return out[:, 0], out[:, 1]
 
 
 def split_range(seq_len: int) -> tuple[int, int]:

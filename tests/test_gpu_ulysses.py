@@ -1,9 +1,10 @@
 """Multi-GPU parity of the Ulysses DiT block (needs >= 2 GPUs; skipped otherwise).
 
 Two NCCL ranks each run their sequence shard of one DiT block, with the
-exchanges either fused into the kernels as P2P stores (transport "p2p") or
-as NCCL all-to-alls ("nccl"); the gathered result must match the same block
-run on one GPU.  With INT8 (per-token
+exchanges either fused into the kernels as P2P stores (transport "p2p"), as
+NCCL all-to-alls ("nccl"), or with K/V all-gathered instead of any head
+exchange ("allgather", the reference's production scheme); the gathered
+result must match the same block run on one GPU.  With INT8 (per-token
 activation scales) every token sees identical arithmetic on both paths, so the
 match is exact.  With NVFP4 the activation global scales are max-reduced
 across ranks (block.global_amax_), so the sharded run quantises exactly as
@@ -80,6 +81,8 @@ def _worker(rank: int, ws: int, port: int, fmt: str, transport: str, mlp_act: st
     ("nvfp4", "p2p", "swiglu"),
     ("int8_tensorwise", "nccl", "gelu"),
     ("nvfp4", "nccl", "gelu"),
+    ("int8_tensorwise", "allgather", "gelu"),
+    ("nvfp4", "allgather", "swiglu"),
 ])
 def test_ulysses_block_matches_single_gpu(fmt, transport, mlp_act):
     if torch.cuda.device_count() < 2:

@@ -1,6 +1,7 @@
-"""CPU, world_size 2/4 over gloo: the Ulysses exchanges of
-minixmax_h3_b200.ulysses reproduce the reference's layout (ops/ulysses.py)
-bit-for-bit, and a rank that dies is reported by the others as an error."""
+"""CPU, world_size 2/4 over gloo: the Ulysses exchanges and the K/V all-gather
+of minixmax_h3_b200.ulysses reproduce the reference's layouts
+(ops/ulysses.py, runtime/dist.py) bit-for-bit, and a rank that dies is
+reported by the others as an error."""
 from __future__ import annotations
 
 import os
@@ -47,6 +48,11 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
             tq, tk, tv = U.all_to_all_qkv(qkv_full[s0:s1].reshape(s1 - s0, -1).contiguous(), h, d)
             for t, part in ((tq, 0), (tk, 1), (tv, 2)):
                 assert torch.equal(t, O.seq_to_head_local(qkv_full[:, part], ws, rank))
+            # all-gather of K and V (runtime/dist.py:291-312): full tensors in rank order
+            kf = torch.randn(s, h, d, generator=torch.Generator().manual_seed(2))
+            vf = torch.randn(s, h, d, generator=torch.Generator().manual_seed(3))
+            kg, vg = U.all_gather_kv(kf[s0:s1].contiguous(), vf[s0:s1].contiguous())
+            assert torch.equal(kg, kf) and torch.equal(vg, vf)
             segs = [(0, 5, 1), (5, s, 0)]
             assert U.clip_mod_segments(segs, s0, s1) == O.clip_mod_segments(segs, s0, s1)
             results.put((rank, "ok"))
