@@ -289,17 +289,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
+    // (its waits poll without a suspend hint: it is the latency-critical
+    // hand-off from the softmax back to the tensor pipe)
     if (lane == 0) {
-      bool ok = mbar_wait(&bars->q_full, 0, &g_status, 3, abort_flag);
+      bool ok = mbar_wait<true>(&bars->q_full, 0, &g_status, 3, abort_flag);
       tc_fence_after();
       const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + Q_TILE_BYTES)};
       auto wait_k = [&](int j) -> uint32_t {
-        if (!mbar_wait(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return 0u;
+        if (!mbar_wait<true>(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return 0u;
         tc_fence_after();
         return smem_u32(sK + (j % KST) * KV_TILE_BYTES);
       };
       auto wait_v = [&](int j) -> uint32_t {
-        if (!mbar_wait(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return 0u;
+        if (!mbar_wait<true>(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return 0u;
         tc_fence_after();
         return smem_u32(sV + (j % VST) * KV_TILE_BYTES);
       };
@@ -324,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t p_tmem = tmem + s_col(i);
         const uint32_t o_tmem = tmem + o_col(i);
         for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&bars->p_half[i][h], j & 1, &g_status, 7, abort_flag)) return false;
+          if (!mbar_wait<true>(&bars->p_half[i][h], j & 1, &g_status, 7, abort_flag)) return false;
           tc_fence_after();
 #pragma unroll
           for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {

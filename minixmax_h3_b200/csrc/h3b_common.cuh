@@ -90,17 +90,33 @@ H3B_DEV bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait without a suspend hint: polls without yielding, for a thread whose
+// reaction time is on the critical path (a single MMA-issuing thread).
+H3B_DEV bool mbar_try_wait_spin(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete.  Returns false (and records
 // `site` in *st, raising *abort_flag) when the budget runs out or when another
 // warp of the CTA already aborted.
+template <bool SPIN = false>
 H3B_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, H3bDeviceStatus* st, int site,
                        volatile int* abort_flag) {
   const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
+  auto poll = [&]() { return SPIN ? mbar_try_wait_spin(addr, parity) : mbar_try_wait(addr, parity); };
+  if (poll()) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (poll()) return true;
     if ((++spins & 255u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (globaltimer_ns() - t0 > H3B_WAIT_NS) {
