@@ -1,8 +1,9 @@
 // Row-wise elementwise kernels of the DiT block (HBM-bound).
 //
 //  * qk_rmsnorm_rope: q/k RMSNorm + split-half RoPE in one pass over each
-//    (token, head) row, the rotation table built on the fly from the token's
-//    (t, h, w) grid position (ops/rope.py:7-55, model/dit.py:746-752).  The
+//    token's head rows, the rotation table built on the fly from the token's
+//    (t, h, w) grid position, once per token (ops/rope.py:7-55,
+//    model/dit.py:746-752).  The
 //    rotation uses the reference's bf16 arithmetic: bf16 cos/sin table, each
 //    product and the sum rounded to bf16.
 //  * rmsnorm_modulate: RMSNorm(hidden) then h*(1+scale)+shift with the
@@ -14,59 +15,88 @@
 
 namespace {
 
-// One warp per (token, head) row of 128 bf16: lane l owns d = 4l..4l+3.
+// One warp per token; lane l owns d = 4l..4l+3 of every 128-element head
+// row.  The token's rotation (bf16 cos/sin of its 64 angles) is computed once
+// and applied to all heads of q and k, ROWS head rows in flight at a time.
+template <int ROWS>
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t s_len, int heads, int64_t seq_stride,
     int64_t head_stride, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
     const float* __restrict__ pos, int64_t pos_offset, const float* __restrict__ inv_freq, int n_t, int n_h) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int64_t rows = s_len * heads * (k != nullptr ? 2 : 1);
-  if (row >= rows) return;
-  const int64_t per = s_len * heads;
-  const bool is_k = row >= per;
-  const int64_t r = is_k ? row - per : row;
-  const int64_t s = r / heads;
-  const int h = static_cast<int>(r - s * heads);
-  __nv_bfloat16* base = (is_k ? k : q) + s * seq_stride + static_cast<int64_t>(h) * head_stride;
-  const __nv_bfloat16* w = is_k ? kw : qw;
-
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (s >= s_len) return;  // warp-uniform
   // element j (lane < 16: j = 4*lane.. in the first half; lane >= 16: second half)
-  const uint2 raw = *reinterpret_cast<const uint2*>(base + lane * 4);
-  float x[4] = {bf16lo_to_f32(raw.x), bf16hi_to_f32(raw.x), bf16lo_to_f32(raw.y), bf16hi_to_f32(raw.y)};
-  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-  ss = warp_sum(ss);
-  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, 128.0f) + eps));
-  const uint2 wraw = *reinterpret_cast<const uint2*>(w + lane * 4);
-  const float wv[4] = {bf16lo_to_f32(wraw.x), bf16hi_to_f32(wraw.x), bf16lo_to_f32(wraw.y), bf16hi_to_f32(wraw.y)};
-  float n[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) n[e] = bf16r(__fmul_rn(__fmul_rn(x[e], rstd), wv[e]));
-  // partner element j +- 64 lives in lane +- 16, same slot
-  float p[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) p[e] = __shfl_xor_sync(0xffffffffu, n[e], 16);
   const float* ps = pos + (pos_offset + s) * 3;
   const bool first = lane < 16;
-  float out[4];
+  float c[4], sn[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int jj = (lane & 15) * 4 + e;  // frequency index 0..63
     const int axis = jj < n_t ? 0 : (jj < n_t + n_h ? 1 : 2);
     const float ang = __fmul_rn(ps[axis], inv_freq[jj]);
-    const float c = bf16r(cosf(ang));
-    const float sn = bf16r(sinf(ang));
-    // first half:  c*x[j] + (-s)*x[j+64];  second half: s*x[j] + c*x[j+64]
-    if (first) {
-      out[e] = bf16r(bf16r(c * n[e]) + bf16r(-sn * p[e]));
-    } else {
-      out[e] = bf16r(bf16r(sn * p[e]) + bf16r(c * n[e]));
+    c[e] = bf16r(cosf(ang));
+    sn[e] = bf16r(sinf(ang));
+  }
+  float wq[4], wk[4];
+  {
+    const uint2 a = *reinterpret_cast<const uint2*>(qw + lane * 4);
+    wq[0] = bf16lo_to_f32(a.x), wq[1] = bf16hi_to_f32(a.x), wq[2] = bf16lo_to_f32(a.y), wq[3] = bf16hi_to_f32(a.y);
+    if (k != nullptr) {
+      const uint2 b = *reinterpret_cast<const uint2*>(kw + lane * 4);
+      wk[0] = bf16lo_to_f32(b.x), wk[1] = bf16hi_to_f32(b.x), wk[2] = bf16lo_to_f32(b.y), wk[3] = bf16hi_to_f32(b.y);
     }
   }
-  uint2 o;
-  o.x = pack_bf16x2(out[0], out[1]);
-  o.y = pack_bf16x2(out[2], out[3]);
-  *reinterpret_cast<uint2*>(base + lane * 4) = o;
+  const int rows = heads * (k != nullptr ? 2 : 1);  // q heads, then k heads
+  for (int r0 = 0; r0 < rows; r0 += ROWS) {
+    uint2 raw[ROWS];
+    __nv_bfloat16* base[ROWS];
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+      const int r = r0 + u;
+      if (r < rows) {
+        const bool is_k = r >= heads;
+        const int h = is_k ? r - heads : r;
+        base[u] = (is_k ? k : q) + s * seq_stride + static_cast<int64_t>(h) * head_stride;
+        raw[u] = *reinterpret_cast<const uint2*>(base[u] + lane * 4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+      const int r = r0 + u;
+      if (r >= rows) break;  // warp-uniform
+      const float* w = r >= heads ? wk : wq;
+      float x[4] = {bf16lo_to_f32(raw[u].x), bf16hi_to_f32(raw[u].x), bf16lo_to_f32(raw[u].y),
+                    bf16hi_to_f32(raw[u].y)};
+      float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+      ss = warp_sum(ss);
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, 128.0f) + eps));
+      float n[4];
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const float2 t = bf16r2(__fmul_rn(__fmul_rn(x[e], rstd), w[e]), __fmul_rn(__fmul_rn(x[e + 1], rstd), w[e + 1]));
+        n[e] = t.x;
+        n[e + 1] = t.y;
+      }
+      // partner element j +- 64 lives in lane +- 16, same slot
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p[e] = __shfl_xor_sync(0xffffffffu, n[e], 16);
+      // first half:  c*x[j] + (-s)*x[j+64];  second half: s*x[j] + c*x[j+64]
+      // (each product and the sum rounded to bf16; two elements per conversion)
+      uint32_t ow[2];
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const float2 a = first ? bf16r2(c[e] * n[e], c[e + 1] * n[e + 1]) : bf16r2(sn[e] * p[e], sn[e + 1] * p[e + 1]);
+        const float2 b = first ? bf16r2(-sn[e] * p[e], -sn[e + 1] * p[e + 1]) : bf16r2(c[e] * n[e], c[e + 1] * n[e + 1]);
+        ow[e >> 1] = pack_bf16x2(a.x + b.x, a.y + b.y);
+      }
+      uint2 o;
+      o.x = ow[0];
+      o.y = ow[1];
+      *reinterpret_cast<uint2*>(base[u] + lane * 4) = o;
+    }
+  }
 }
 
 // CTAs of 256 threads stride over rows; a row is held in registers (<= MAXV
@@ -129,19 +159,17 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
       uint32_t outw[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float o2[2];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const float xv = half ? bf16hi_to_f32(xu[e]) : bf16lo_to_f32(xu[e]);
-          const float wvv = half ? bf16hi_to_f32(wu[e]) : bf16lo_to_f32(wu[e]);
-          const float shv = half ? bf16hi_to_f32(shu[e]) : bf16lo_to_f32(shu[e]);
-          const float scv = half ? bf16hi_to_f32(scu[e]) : bf16lo_to_f32(scu[e]);
-          const float nrm = bf16r(__fmul_rn(__fmul_rn(xv, rstd), wvv));
-          const float mod = modulate ? bf16r(bf16r(nrm * bf16r(1.0f + scv)) + shv) : nrm;
-          amax = fmaxf(amax, fabsf(mod));
-          o2[half] = mod;
+        // both bf16 halves of the 32-bit word together: one packed rounding per step
+        const float2 nrm = bf16r2(__fmul_rn(__fmul_rn(bf16lo_to_f32(xu[e]), rstd), bf16lo_to_f32(wu[e])),
+                                  __fmul_rn(__fmul_rn(bf16hi_to_f32(xu[e]), rstd), bf16hi_to_f32(wu[e])));
+        float2 mod = nrm;
+        if (modulate) {
+          const float2 s1 = bf16r2(1.0f + bf16lo_to_f32(scu[e]), 1.0f + bf16hi_to_f32(scu[e]));
+          const float2 t = bf16r2(nrm.x * s1.x, nrm.y * s1.y);
+          mod = bf16r2(t.x + bf16lo_to_f32(shu[e]), t.y + bf16hi_to_f32(shu[e]));
         }
-        outw[e] = pack_bf16x2(o2[0], o2[1]);
+        amax = fmax3(amax, fabsf(mod.x), fabsf(mod.y));
+        outw[e] = pack_bf16x2(mod.x, mod.y);
       }
       *reinterpret_cast<uint4*>(hr + vi * 8) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
     }
@@ -200,10 +228,10 @@ extern "C" int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, i
   if ((reinterpret_cast<uintptr_t>(q) & 7u) || (k != nullptr && (reinterpret_cast<uintptr_t>(k) & 7u)))
     return H3B_ERR_ALIGN;
   if (s == 0) return H3B_OK;
-  const int64_t rows = s * heads * (k != nullptr ? 2 : 1);
-  const int64_t blocks = (rows + 7) / 8;
+  if (heads > 65535) return H3B_ERR_SHAPE;
+  const int64_t blocks = (s + 7) / 8;  // one warp per token
   if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
-  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  qk_rmsnorm_rope_kernel<4><<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), s, static_cast<int>(heads), seq_stride,
       head_stride, static_cast<const __nv_bfloat16*>(q_weight), static_cast<const __nv_bfloat16*>(k_weight), eps,
       pos, pos_offset, inv_freq, n_t, n_h);

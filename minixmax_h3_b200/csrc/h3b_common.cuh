@@ -451,6 +451,12 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t m, uint32_t n) {
 // ----------------------------------------------------------------------------
 // fp32 -> nearest-even bf16 -> fp32 (one rounding step of a bf16 computation).
 H3B_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+// The same rounding for two values with one packed conversion.
+H3B_DEV float2 bf16r2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
 H3B_DEV float bf16lo_to_f32(uint32_t v) { return __uint_as_float(v << 16); }
 H3B_DEV float bf16hi_to_f32(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

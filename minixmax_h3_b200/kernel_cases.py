@@ -6,6 +6,8 @@
     python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8_convrot --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases qk_rope --seq 131072 --heads 24
+    python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate --m 131072 --k 3072
 
 Each case allocates its inputs once, launches the kernel `--warmup` times,
 then `--iters` times between CUDA events on the launching stream, and prints
@@ -39,7 +41,7 @@ def _time(fn, warmup: int, iters: int) -> float:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8",
-                                       "quant_i8_convrot"])
+                                       "quant_i8_convrot", "qk_rope", "rmsnorm_modulate"])
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--heads", type=int, default=24)
     ap.add_argument("--m", type=int, default=8192)
@@ -72,6 +74,30 @@ def main() -> None:
             ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, out=out), a.warmup, a.iters)
         flops = 2.0 * a.m * a.n * a.k
         rec.update(m=a.m, n=a.n, k=a.k, ms=ms, tflops=flops / ms / 1e9, flops=flops)
+    elif a.case == "qk_rope":
+        # q and k views of a packed [S, 3, H, 128] QKV buffer, in place
+        from .block import RopeSpec
+        qkv = torch.randn(a.seq, 3, a.heads, 128, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.ones(128, dtype=torch.bfloat16, device=dev)
+        side = int(round((a.seq / 4) ** 0.5))
+        t_len = (a.seq + side * side - 1) // (side * side)
+        pos = RopeSpec.grid_positions(t_len, side, side)[: a.seq]
+        rope = RopeSpec.build(pos, device=dev)
+        ms = _time(lambda: ops.qk_rmsnorm_rope(qkv[:, 0], qkv[:, 1], w, w, 1e-6, rope.pos, 0, rope.inv_freq,
+                                               rope.n_t, rope.n_h), a.warmup, a.iters)
+        nbytes = 2 * 2 * a.seq * a.heads * 128 * 2 + a.seq * 3 * 4  # q, k read + written; positions
+        rec.update(seq=a.seq, heads=a.heads, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
+    elif a.case == "rmsnorm_modulate":
+        x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.ones(a.k, dtype=torch.bfloat16, device=dev)
+        tab = (torch.randn(2, 2 * a.k, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        row_sel = torch.zeros(a.m, dtype=torch.int32, device=dev)
+        out = torch.empty_like(x)
+        amax = torch.zeros(1, dtype=torch.float32, device=dev)
+        ms = _time(lambda: ops.rmsnorm_modulate(x, w, tab[:, : a.k], tab[:, a.k:], 1e-6, row_sel=row_sel, out=out,
+                                                amax_out=amax), a.warmup, a.iters)
+        nbytes = 2 * a.m * a.k * 2 + 4 * a.m  # x read, h written, row indices
+        rec.update(m=a.m, k=a.k, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
     else:
         x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
         if a.case == "quant_nvfp4":
