@@ -4,11 +4,11 @@
 //                  y = acc * xs[m] * ws[n] (+ bias[n])  — the semantics of
 //                  torch_npu.npu_quant_matmul at ops/int8_convrot.py:86-93.
 //   NVFP4 (W4A4):  kind::mxf4nvf4.block_scale.block16, e2m1 operands with one
-//                  ue4m3 scale per 16 elements copied smem -> TMEM with
-//                  tcgen05.cp, epilogue y = acc * a_gs * w_gs (+ bias[n]).
+//                  ue4m3 scale per 16 elements written into TMEM by four
+//                  scale-writer warps, epilogue y = acc * a_gs * w_gs (+ bias[n]).
 //
-// Structure (persistent, one CTA per SM; for M > 128 the CTAs work in
-// clusters of two on 256 x BN tiles with cta_group::2 MMAs):
+// Structure (persistent, one CTA per SM; INT8 GEMMs with M > 128 work in
+// clusters of two CTAs on 256 x BN tiles with cta_group::2 MMAs):
 //   warp 0      TMA producer: this CTA's 128 rows of A, its BN/PAIR rows of B
 //               (+ scale factors) into a 4- or 6-deep smem ring.  In a pair,
 //               both CTAs' copies complete on the leader's full barrier,
@@ -22,16 +22,25 @@
 //               GELU / SwiGLU / gate-residual / seq->head scatter, bf16
 //               blocks staged in 64B-swizzled shared memory and written by
 //               TMA stores; each warp releases the accumulator to the leader.
-// Accumulators are double-buffered in TMEM (columns 0 and 256), so the MMAs
+//   warps 6-9   (NVFP4) scale writers, one per TMEM lane quadrant: each
+//               loads a slab's scales from shared memory into registers one
+//               slab ahead, stores them into its 32 TMEM lanes with
+//               tcgen05.st and arrives on the slab's full barrier, so the MMA
+//               thread waits once per slab and issues nothing but MMAs.
+// The single issuing thread is the MMA pipe's feeder: each tcgen05.mma,
+// tcgen05.cp and barrier poll it executes costs issue time, and at 4 NVFP4
+// MMAs of 128x192x64 per 384-cycle slab a thread that also issued the 12
+// scale copies of a slab (about 45 cycles each) could not keep the pipe fed.
+// Accumulators are double-buffered in TMEM (BN columns apart), so the MMAs
 // of tile t+1 run while the epilogue drains tile t:
 //   INT8:  BN = 256.
-//   NVFP4: BN = 192, plus a 2-slot scale-factor ring at columns 192 and 448
-//          (48 columns per slot), refilled by tcgen05.cp in issue order
-//          behind the MMAs that read it.  A 192-row N tile starts either
-//          on a 128-row scale block (even tiles) or 64 rows into one (odd
-//          tiles): the two blocks covering it are copied and the MMA's SFB
-//          address skips 2 TMEM columns (= 64 rows) for odd tiles.  In a
-//          pair each CTA copies its own A scales and the tile's B scales.
+//   NVFP4: BN = 192, plus two 48-column scale slots at columns 384 and 432
+//          (slab it uses slot it&1; the writers refill it once the MMAs of
+//          slab it-2 have completed, seen through that slab's empty
+//          barrier).  A slot holds, per K-step j, 4 columns of A scales
+//          (the four-quadrant image of the blocked 128x4 atom: lane 32q+b,
+//          column 4j+a = scales of row 32a+b) and 8 columns of B scales
+//          (column 8j+i = scales of tile rows 32i+b in every quadrant).
 // Operands are K-major with the 128-byte swizzle.  No load uses cluster
 // multicast.  Every wait is bounded; both CTAs of a pair stay resident until
 // a final cluster barrier.
@@ -49,9 +58,10 @@ constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
 constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
 constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
 constexpr int EPI_THREADS = 128;
-constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int SF_THREADS = 128;  // NVFP4: four scale-factor writer warps, one per TMEM lane quadrant
 constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 staging buffer
-constexpr int ACC_STRIDE = 256;           // TMEM columns between the two accumulators
+constexpr int SF_SLOTS = 2;               // NVFP4 scale slots in TMEM, one K slab each
+constexpr int SF_SLOT_COLS = 48;          // 16 (A: 4 K-steps x 4) + 32 (B: 4 K-steps x 8)
 
 enum Kind { KIND_I8 = 0, KIND_NVF4 = 1 };
 enum OutMode { OUT_BF16 = 0, OUT_I32 = 1, OUT_SEQ2HEAD = 2 };
@@ -93,25 +103,36 @@ struct Cfg {
   static constexpr int B_ROWS = BN / PAIR;                 // B rows staged by this CTA
   static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int STAGES = PAIR == 1 ? 4 : 6;
-  static constexpr int SF_COLS_PER_SLOT = 48;  // 16 (A) + 32 (B)
+  static constexpr int ACC_STRIDE = BN;        // TMEM columns between the two accumulators
+  static constexpr int SF_BASE = 2 * BN;       // NVFP4 scale slots follow the accumulators
   static constexpr int TMEM_COLS = 512;
   static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
-  static constexpr int TX_BYTES = PAIR * STAGE_BYTES;  // the leader's full barrier counts both CTAs' bytes
+  // The leader's full barrier counts both CTAs' A and B bytes (and, for
+  // NVFP4, the four scale writers' arrivals); scale bytes land on sf_ready.
+  static constexpr int TX_BYTES = PAIR * (A_BYTES + B_BYTES);
+  static constexpr int FULL_ARRIVALS = KIND == KIND_NVF4 ? 1 + SF_THREADS / 32 : 1;
+  static constexpr int THREADS = 64 + EPI_THREADS + (KIND == KIND_NVF4 ? SF_THREADS : 0);
   static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
   static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM * PAIR, BN) : idesc_nvf4(BM * PAIR, BN);
   static_assert(STAGES <= MAX_STAGES, "barrier arrays");
-  static_assert(BN <= ACC_STRIDE, "accumulator overlap");
-  static_assert(KIND == KIND_I8 || BN + SF_COLS_PER_SLOT <= ACC_STRIDE, "SF slot overlaps an accumulator");
+  static_assert(KIND == KIND_I8 || PAIR == 1, "NVFP4 runs single-CTA tiles");
+  static_assert(2 * ACC_STRIDE <= TMEM_COLS, "accumulators exceed TMEM");
+  static_assert(KIND == KIND_I8 || SF_BASE + SF_SLOTS * SF_SLOT_COLS <= TMEM_COLS, "scale slots exceed TMEM");
   static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 };
 
-// TMEM column of scale-factor slot `slot` (NVFP4): just past each accumulator.
-H3B_DEV uint32_t sf_slot_col(int slot) { return 192u + static_cast<uint32_t>(slot) * ACC_STRIDE; }
+// TMEM column of NVFP4 scale slot `slot` (A scales at +4j, B scales at
+// +16+8j for K-step j).
+template <int KIND, int PAIR>
+H3B_DEV uint32_t sf_slot_col(int slot) {
+  return static_cast<uint32_t>(Cfg<KIND, PAIR>::SF_BASE + slot * SF_SLOT_COLS);
+}
 
 struct __align__(8) Barriers {
   uint64_t full[MAX_STAGES];
   uint64_t empty[MAX_STAGES];
+  uint64_t sf_ready[MAX_STAGES];  // NVFP4: the scale bytes of stage s landed in shared memory
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -125,16 +146,17 @@ constexpr size_t smem_bytes() {
   return 1024 /*alignment slack*/ + static_cast<size_t>(Cfg<KIND, PAIR>::STAGES) * Cfg<KIND, PAIR>::STAGE_BYTES +
          4 * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
 }
-static_assert(smem_bytes<KIND_NVF4, 2>() <= 227 * 1024 && smem_bytes<KIND_I8, 2>() <= 227 * 1024 &&
-                  smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 && smem_bytes<KIND_I8, 1>() <= 227 * 1024,
+static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
+                  smem_bytes<KIND_I8, 1>() <= 227 * 1024,
               "shared memory budget");
 
 H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
 // Lane 0 waits, the verdict is broadcast so the whole warp stays converged.
+template <bool SPIN = false>
 H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
   int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait<SPIN>(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -144,10 +166,9 @@ H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* a
 H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
 template <int KIND, int PAIR>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ PeerMaps peers,
-                const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                 const GemmArgs args) {
   using C = Cfg<KIND, PAIR>;
   constexpr int BN = C::BN;
@@ -174,8 +195,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->full[s], C::FULL_ARRIVALS);
       mbar_init(&bars->empty[s], 1);
+      mbar_init(&bars->sf_ready[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
@@ -231,19 +253,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_load_2d_pair(sA + s * A_BYTES, &tmap_a, kb * 128, m0, full_l);
             tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, kb * 128, n0 + static_cast<int>(rank) * C::B_ROWS,
                              full_l);
-            if constexpr (KIND == KIND_NVF4) {
-              // Scale rows of 512 bytes (one 128-row block x 4 scale columns):
-              // A: this CTA's block, B: the tile's two 128-row blocks.
-              const int ncb = args.k / 64;
-              const int nb0 = n0 / 128;
-              const int nb1 = (nb0 + 1) * 128 < args.n ? nb0 + 1 : nb0;
-              tma_load_2d_pair(sSFA + s * SFA_BYTES, &tmap_sfa, 0, (m0 / 128) * ncb + kb * 4, full_l);
-              tma_load_2d_pair(sSFB + s * SFB_BYTES, &tmap_sfb, 0, nb0 * ncb + kb * 4, full_l);
-              tma_load_2d_pair(sSFB + s * SFB_BYTES + SFB_BYTES / 2, &tmap_sfb, 0, nb1 * ncb + kb * 4, full_l);
-            }
             continue;
           }
-          mbar_arrive_expect_tx(&bars->full[s], C::STAGE_BYTES);
+          mbar_arrive_expect_tx(&bars->full[s], C::TX_BYTES);
           tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * 128, m0, &bars->full[s]);
           tma_load_2d(sB + s * C::B_BYTES, &tmap_b, kb * 128, n0, &bars->full[s]);
           if constexpr (KIND == KIND_NVF4) {
@@ -256,9 +268,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int nb1 = (nb0 + 1) * 128 < args.n ? nb0 + 1 : nb0;
             const uint8_t* sfb0 = args.w_sf + ((static_cast<int64_t>(nb0) * ncb) + kb * 4) * 512;
             const uint8_t* sfb1 = args.w_sf + ((static_cast<int64_t>(nb1) * ncb) + kb * 4) * 512;
-            bulk_load(sSFA + s * SFA_BYTES, sfa, SFA_BYTES, &bars->full[s]);
-            bulk_load(sSFB + s * SFB_BYTES, sfb0, SFB_BYTES / 2, &bars->full[s]);
-            bulk_load(sSFB + s * SFB_BYTES + SFB_BYTES / 2, sfb1, SFB_BYTES / 2, &bars->full[s]);
+            mbar_arrive_expect_tx(&bars->sf_ready[s], C::SF_STAGE_BYTES);
+            bulk_load(sSFA + s * SFA_BYTES, sfa, SFA_BYTES, &bars->sf_ready[s]);
+            bulk_load(sSFB + s * SFB_BYTES, sfb0, SFB_BYTES / 2, &bars->sf_ready[s]);
+            bulk_load(sSFB + s * SFB_BYTES + SFB_BYTES / 2, sfb1, SFB_BYTES / 2, &bars->sf_ready[s]);
           }
         }
       }
@@ -268,7 +281,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           // so no copy is still writing this CTA's shared memory at exit.
           const int consumed = *reinterpret_cast<volatile int*>(&bars->consumed);
           for (int j = consumed; j < it; ++j) {
-            mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+            if constexpr (KIND == KIND_NVF4) {
+              // full[] also counts the writers' arrivals: wait for the
+              // scale bytes, then give the A/B copies a bounded 200 us.
+              mbar_wait(&bars->sf_ready[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+            } else {
+              mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, &g_status, 9, nullptr);
+            }
+          }
+          if constexpr (KIND == KIND_NVF4) {
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 200000ull) {
+            }
           }
         } else {
           // The peer's copies complete on the leader's barriers, which it
@@ -290,17 +314,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters, ++local) {
         const int buf = local & 1;
         const int use = local >> 1;
-        if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
+        if (use > 0 && !mbar_wait<false, PAIR == 2>(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * ACC_STRIDE;
-        // Odd 192-wide N tiles start 64 rows into their first scale block.
-        const uint32_t sfb_skip = (KIND == KIND_NVF4 && ((tile % n_tiles) & 1)) ? 2u : 0u;
+        const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
-          if (!mbar_wait(&bars->full[s], (it / STAGES) & 1, &g_status, 3, abort_flag)) {
+          if (!mbar_wait<true>(&bars->full[s], (it / STAGES) & 1, &g_status, 3, abort_flag)) {
             ok = false;
             break;
           }
@@ -317,34 +339,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
             }
           } else {
-            // tcgen05.cp and tcgen05.mma issued by this one thread execute in
-            // issue order in the tensor pipe, so refilling slot it&1 cannot
-            // overtake the MMAs of slab it-2 that read it (the pattern
-            // CUTLASS's block-scaled mainloop relies on with a single slot).
-            const uint32_t sf_col = tmem_base + sf_slot_col(it & 1);
-            auto cp = [&](uint32_t taddr, uint64_t desc) {
-              if constexpr (PAIR == 2)
-                tc_cp_32x128b_x4_pair(taddr, desc);  // each CTA: its own scales -> its own TMEM
-              else
-                tc_cp_32x128b_x4(taddr, desc);
-            };
+            // full[s] also means: this slab's scales are in TMEM slot it&1
+            const uint32_t sf_col = tmem_base + sf_slot_col<KIND, PAIR>(it & 1);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              cp(sf_col + j * 4, sdesc_plain_rows16(smem_u32(sSFA + s * SFA_BYTES + j * 512)));
-              cp(sf_col + 16 + j * 8, sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + j * 512)));
-              cp(sf_col + 16 + j * 8 + 4, sdesc_plain_rows16(smem_u32(sSFB + s * SFB_BYTES + SFB_BYTES / 2 + j * 512)));
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if constexpr (PAIR == 2)
-                mma_nvf4_ss_pair(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
-                                 sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
-              else
-                mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
-                            sf_col + 16 + j * 8 + sfb_skip, (kb | j) != 0);
-            }
+            for (int j = 0; j < 4; ++j)
+              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4, sf_col + 16 + j * 8,
+                          (kb | j) != 0);
           }
-          // slot reusable (in both CTAs) once these MMAs have read it
+          // stage reusable (in both CTAs) once these MMAs have read it
           if constexpr (PAIR == 2)
             tc_commit_pair_mc(&bars->empty[s], 0x3);
           else
@@ -362,6 +364,63 @@ __global__ void __launch_bounds__(THREADS, 1)
       else
         tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
+    }
+  } else if (KIND == KIND_NVF4 && warp >= 2 + EPI_THREADS / 32) {
+    // ------------------------------------------------------ scale writers
+    // Warp q writes TMEM lanes 32q..32q+31 of slot it&1 for slab it:
+    //   A part, column 4j+a: word a of row b of blocked chunk j (the four
+    //     scales of A row 32a+b for K-step j; quadrant q reads column 4j+q);
+    //   B part, column 8j+i (i < 6): the scales of tile row 32i+b for K-step
+    //     j, the same in every quadrant.  A 192-row tile starts on a 128-row
+    //     scale block (even tiles) or 64 rows into one (odd tiles), so tile
+    //     row group i is word (g & 3) of block g >> 2, g = i (+2 if odd).
+    // The slab's scales are read from shared memory one slab ahead, while
+    // the previous slab's stores are in flight.
+    const int quad = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int my_tiles = cluster < num_tiles ? (num_tiles - 1 - cluster) / n_clusters + 1 : 0;
+    const int total = my_tiles * nk;
+    uint4 nx[12];  // slab it's scales: A chunks 0-3, then B (block h, chunk j) at 4 + 2j + h
+    auto load = [&](int slab) -> bool {
+      const int s = slab % STAGES;
+      if (!warp_wait<true>(&bars->sf_ready[s], (slab / STAGES) & 1, 7, abort_flag)) return false;
+      const uint8_t* sfa = sSFA + s * SFA_BYTES + lane * 16;
+      const uint8_t* sfb = sSFB + s * SFB_BYTES + lane * 16;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        nx[j] = *reinterpret_cast<const uint4*>(sfa + j * 512);
+        nx[4 + 2 * j] = *reinterpret_cast<const uint4*>(sfb + j * 512);
+        nx[5 + 2 * j] = *reinterpret_cast<const uint4*>(sfb + SFB_BYTES / 2 + j * 512);
+      }
+      return true;
+    };
+    bool ok = total > 0 ? load(0) : true;
+    for (int it = 0; it < total && ok; ++it) {
+      const int tile = cluster + (it / nk) * n_clusters;
+      const bool odd = ((tile % n_tiles) & 1) != 0;
+      uint32_t ra[16], rb[32];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ra[4 * j] = nx[j].x, ra[4 * j + 1] = nx[j].y, ra[4 * j + 2] = nx[j].z, ra[4 * j + 3] = nx[j].w;
+        const uint32_t w[8] = {nx[4 + 2 * j].x, nx[4 + 2 * j].y, nx[4 + 2 * j].z, nx[4 + 2 * j].w,
+                               nx[5 + 2 * j].x, nx[5 + 2 * j].y, nx[5 + 2 * j].z, nx[5 + 2 * j].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rb[8 * j + i] = odd ? (i < 6 ? w[i + 2] : 0u) : w[i];
+      }
+      // slot it&1 was last read by the MMAs of slab it-2
+      if (it >= 2 && !warp_wait<true>(&bars->empty[(it - 2) % STAGES], ((it - 2) / STAGES) & 1, 6, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR>(it & 1);
+      tmem_st16(t, ra);
+      tmem_st32(t + 16, rb);
+      if (it + 1 < total) ok = load(it + 1);  // overlaps the stores in flight
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->full[it % STAGES]);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -401,7 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         row_scale = (*args.a_gs) * (*args.w_gs);
       }
-      const uint32_t t_row = tmem_base + buf * ACC_STRIDE + (static_cast<uint32_t>(quad * 32) << 16);
+      const uint32_t t_row = tmem_base + buf * C::ACC_STRIDE + (static_cast<uint32_t>(quad * 32) << 16);
       // acc -> fp32 output of column `col` before any activation.  Explicit
       // _rn ops: no FMA contraction, so the INT8 epilogue is bit-reproducible
       // as (acc*xs)*ws + bias in fp32.
@@ -546,7 +605,7 @@ template <int KIND, int PAIR>
 int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                   cudaStream_t st, const PeerMaps* peer_maps) {
   using C = Cfg<KIND, PAIR>;
-  CUtensorMap ta, tb, ty, tsfa, tsfb;
+  CUtensorMap ta, tb, ty;
   int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != H3B_OK) return rc;
@@ -561,19 +620,6 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
     if (rc != H3B_OK) return rc;
   } else {
     ty = ta;  // the int32 and scatter paths never use this map
-  }
-  tsfa = ta;
-  tsfb = ta;
-  if (KIND == KIND_NVF4 && PAIR == 2) {
-    // Blocked scales as rows of 512 bytes (64 x u64): one 128-row block x 4
-    // scale columns per row; a K slab's scales are 4 consecutive rows.
-    const int64_t ncb = args.k / 64;
-    rc = h3b::encode_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT64, args.a_sf, 64, (args.m + 127) / 128 * ncb, 512, 64,
-                        4, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != H3B_OK) return rc;
-    rc = h3b::encode_2d(&tsfb, CU_TENSOR_MAP_DATA_TYPE_UINT64, args.w_sf, 64, (args.n + 127) / 128 * ncb, 512, 64,
-                        4, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != H3B_OK) return rc;
   }
   const size_t smem = smem_bytes<KIND, PAIR>();
   static bool attr_set = false;
@@ -593,7 +639,7 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
   if constexpr (PAIR == 2) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * units));
-    cfg.blockDim = dim3(THREADS);
+    cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -603,10 +649,10 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, 2>, ta, tb, ty, pm, tsfa, tsfb, args) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, 2>, ta, tb, ty, pm, args) != cudaSuccess)
       return H3B_ERR_LAUNCH;
   } else {
-    gemm_kernel<KIND, 1><<<units, THREADS, smem, st>>>(ta, tb, ty, pm, tsfa, tsfb, args);
+    gemm_kernel<KIND, 1><<<units, C::THREADS, smem, st>>>(ta, tb, ty, pm, args);
   }
   return h3b::launch_status();
 }
@@ -616,7 +662,9 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
 template <int KIND>
 int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                 cudaStream_t st, const PeerMaps* peer_maps = nullptr) {
-  if (args.m > BM) return launch_gemm_t<KIND, 2>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  if constexpr (KIND == KIND_I8) {
+    if (args.m > BM) return launch_gemm_t<KIND, 2>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  }
   return launch_gemm_t<KIND, 1>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
 }
 

@@ -104,14 +104,32 @@ H3B_DEV bool mbar_try_wait_spin(uint32_t bar_addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Cluster-scope acquire: for a barrier that threads of the other CTA of a
+// cluster arrive on (their release.cluster arrivals pair with it).
+H3B_DEV bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete.  Returns false (and records
 // `site` in *st, raising *abort_flag) when the budget runs out or when another
-// warp of the CTA already aborted.
-template <bool SPIN = false>
+// warp of the CTA already aborted.  SPIN: poll without a suspend hint;
+// CLUSTER: cluster-scope acquire (polls too).
+template <bool SPIN = false, bool CLUSTER = false>
 H3B_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, H3bDeviceStatus* st, int site,
                        volatile int* abort_flag) {
   const uint32_t addr = smem_u32(bar);
-  auto poll = [&]() { return SPIN ? mbar_try_wait_spin(addr, parity) : mbar_try_wait(addr, parity); };
+  auto poll = [&]() {
+    return CLUSTER ? mbar_try_wait_cluster(addr, parity)
+                   : (SPIN ? mbar_try_wait_spin(addr, parity) : mbar_try_wait(addr, parity));
+  };
   if (poll()) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
@@ -382,6 +400,11 @@ H3B_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+H3B_DEV void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 H3B_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
