@@ -22,15 +22,19 @@
 //               GELU / SwiGLU / gate-residual / seq->head scatter, bf16
 //               blocks staged in 64B-swizzled shared memory and written by
 //               TMA stores; each warp releases the accumulator to the leader.
-//   warps 6-9   (NVFP4) scale writers, one per TMEM lane quadrant: each
-//               loads a slab's scales from shared memory into registers one
-//               slab ahead, stores them into its 32 TMEM lanes with
-//               tcgen05.st and arrives on the slab's full barrier, so the MMA
-//               thread waits once per slab and issues nothing but MMAs.
-// The single issuing thread is the MMA pipe's feeder: each tcgen05.mma,
-// tcgen05.cp and barrier poll it executes costs issue time, and at 4 NVFP4
-// MMAs of 128x192x64 per 384-cycle slab a thread that also issued the 12
-// scale copies of a slab (about 45 cycles each) could not keep the pipe fed.
+//   warps 6-13  (NVFP4) scale writers, two per TMEM lane quadrant (a warp
+//               reaches only the lanes of quadrant warp % 4), taking even
+//               and odd slabs: each loads its slab's scales from shared
+//               memory into registers ahead of time, stores them into its 32
+//               TMEM lanes with tcgen05.st and arrives on the slab's full
+//               barrier, so the MMA thread waits once per slab and issues
+//               nothing but MMAs.  (With one writer per quadrant, the ones
+//               sharing a scheduler with the producer or the MMA thread fell
+//               a slab behind and paced the pipe.)
+// The single issuing thread is the MMA pipe's feeder: a block-scaled MMA
+// takes ~55 cycles to issue, a commit ~75 and a barrier poll ~80, so 4 NVFP4
+// MMAs of 128x192x64 per 384-cycle slab leave it no room for the 12 scale
+// copies (tcgen05.cp, ~45 cycles of issue each) a slab would need.
 // Accumulators are double-buffered in TMEM (BN columns apart), so the MMAs
 // of tile t+1 run while the epilogue drains tile t:
 //   INT8:  BN = 256.
@@ -58,7 +62,7 @@ constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
 constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
 constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
 constexpr int EPI_THREADS = 128;
-constexpr int SF_THREADS = 128;  // NVFP4: four scale-factor writer warps, one per TMEM lane quadrant
+constexpr int SF_THREADS = 256;  // NVFP4: two scale writer warps per TMEM lane quadrant (even / odd slabs)
 constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 staging buffer
 constexpr int SF_SLOTS = 2;               // NVFP4 scale slots in TMEM, one K slab each
 constexpr int SF_SLOT_COLS = 48;          // 16 (A: 4 K-steps x 4) + 32 (B: 4 K-steps x 8)
@@ -111,7 +115,7 @@ struct Cfg {
   // The leader's full barrier counts both CTAs' A and B bytes (and, for
   // NVFP4, the four scale writers' arrivals); scale bytes land on sf_ready.
   static constexpr int TX_BYTES = PAIR * (A_BYTES + B_BYTES);
-  static constexpr int FULL_ARRIVALS = KIND == KIND_NVF4 ? 1 + SF_THREADS / 32 : 1;
+  static constexpr int FULL_ARRIVALS = KIND == KIND_NVF4 ? 1 + 4 : 1;  // the arm + one writer per quadrant
   static constexpr int THREADS = 64 + EPI_THREADS + (KIND == KIND_NVF4 ? SF_THREADS : 0);
   static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
   static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM * PAIR, BN) : idesc_nvf4(BM * PAIR, BN);
@@ -376,7 +380,11 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     //     row group i is word (g & 3) of block g >> 2, g = i (+2 if odd).
     // The slab's scales are read from shared memory one slab ahead, while
     // the previous slab's stores are in flight.
+    // Two warps per quadrant take alternate slabs (slab parity = slot), so
+    // a writer that shares its scheduler with the producer or the MMA thread
+    // still has two slab periods for each store.
     const int quad = warp & 3;
+    const int parity = (warp - 2 - EPI_THREADS / 32) >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int my_tiles = cluster < num_tiles ? (num_tiles - 1 - cluster) / n_clusters + 1 : 0;
     const int total = my_tiles * nk;
@@ -394,8 +402,8 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       }
       return true;
     };
-    bool ok = total > 0 ? load(0) : true;
-    for (int it = 0; it < total && ok; ++it) {
+    bool ok = parity < total ? load(parity) : true;
+    for (int it = parity; it < total && ok; it += 2) {
       const int tile = cluster + (it / nk) * n_clusters;
       const bool odd = ((tile % n_tiles) & 1) != 0;
       uint32_t ra[16], rb[32];
@@ -416,11 +424,11 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR>(it & 1);
       tmem_st16(t, ra);
       tmem_st32(t + 16, rb);
-      if (it + 1 < total) ok = load(it + 1);  // overlaps the stores in flight
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->full[it % STAGES]);
+      if (it + 2 < total) ok = load(it + 2);
     }
   } else {
     // ------------------------------------------------------------ epilogue
