@@ -327,26 +327,7 @@ H3B_DEV void mma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uin
       "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-H3B_DEV void mma_nvf4_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa_tmem,
-                              uint32_t sfb_tmem, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
-}
-// Each CTA of the pair copies its own shared-memory matrix (same offset) into
-// its own TMEM (issued by the leader).
-H3B_DEV void tc_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc));
-}
 
-// Copy a 32-row x 16-byte smem matrix into TMEM, replicated over the four lane
-// quadrants (the scale-factor layout the block-scaled MMA reads).
-H3B_DEV void tc_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc));
-}
 
 // 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
 H3B_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -400,11 +381,6 @@ H3B_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-H3B_DEV void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
 H3B_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -444,12 +420,6 @@ H3B_DEV uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
 H3B_DEV uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(lbo_bytes >> 4) << 16) |
          (static_cast<uint64_t>(sbo_bytes >> 4) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// Un-swizzled descriptor for tcgen05.cp sources: 8-row x 16-byte core
-// matrices stored contiguously (128 bytes apart).
-H3B_DEV uint64_t sdesc_plain_rows16(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (8ull << 16) | (8ull << 32) | (1ull << 46);
 }
 
 // Instruction descriptors (kind::f16 / kind::i8 share this format).
