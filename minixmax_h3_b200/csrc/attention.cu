@@ -154,8 +154,11 @@ H3B_DEV float2 exp2_poly2(float2 x) {
   return make_float2(__uint_as_float(bx), __uint_as_float(by));
 }
 
-// Pairs (out of every 8) whose exponentials go to the FMA pipe instead of MUFU.
-constexpr int POLY_PAIRS_PER_8 = 3;
+// Pairs (out of every 8) whose exponentials go to the FMA pipe instead of
+// MUFU.  Measured on B200 at S = 32768..131072: 0 -> 1131 / 1074 TFLOP/s,
+// 1 -> 1122 / 1057, 2 -> 1107 / -, 3 -> 1060 / 1020 (24 heads); the
+// softmax's FMA and ALU work already fills those pipes, MUFU has room.
+constexpr int POLY_PAIRS_PER_8 = 0;
 
 // In-place softmax numerator for 64 columns r[0..63] (fp32 S bits in, packed
 // bf16 P out in dst[0..31]): packed fp32x2 FMA, 64 independent exponentials
