@@ -289,6 +289,21 @@ H3B_API int h3b_attention_fwd_head2seq(const void* q, const void* k, const void*
                                        int64_t kv_seq_stride, int64_t kv_head_stride, float scale,
                                        h3b_stream_t stream);
 
+/* Merge of an attention result over one key chunk into a running result
+ * over earlier chunks through the rows' log-sum-exps, in fp32 — the ring
+ * sequence-parallel step of ops/fa_h3.py:141-156 (_merge_lse), used by
+ * ring_attention_lse_bnsd (ops/fa_h3.py:159-218):
+ *   acc <- acc - sigmoid(blk_lse - acc_lse) * (acc - blk)
+ *   acc_lse <- acc_lse - logsigmoid(acc_lse - blk_lse)
+ * acc fp32 and blk bf16 are token-major [s, heads, 128], contiguous; lse
+ * arrays [heads, s] fp32 (natural log, as h3b_attention_fwd writes them).
+ * first != 0 initialises acc / acc_lse from blk / blk_lse.  With out given
+ * (bf16 [s, heads, 128]) the merged rows are written there instead of acc,
+ * and max |out| into amax_out (optional, caller-zeroed fp32).
+ */
+H3B_API int h3b_attention_merge_lse(float* acc, float* acc_lse, const void* blk, const float* blk_lse, int64_t s,
+                                    int64_t heads, int first, void* out, float* amax_out, h3b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

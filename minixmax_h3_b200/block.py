@@ -31,7 +31,7 @@ from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
 from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer,
-                      phase_barrier, split_range, transport)
+                      phase_barrier, ring_attention, split_range, transport)
 
 
 @dataclass
@@ -161,6 +161,7 @@ class Attention(nn.Module):
         if sp and transport() == "p2p":
             return self._forward_p2p(h, rope_freqs, amax_h=amax_h, resid=resid, gate=gate, row_sel=row_sel)
         gather_kv = sp and transport() == "allgather"
+        ring = sp and transport() == "ring"
         qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
         if rope_freqs is not None:
@@ -175,7 +176,15 @@ class Attention(nn.Module):
             ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
                                 pos0, 0, zeros, 64, 0)
         amax_o = torch.zeros(1, dtype=torch.float32, device=h.device)
-        if gather_kv:
+        if ring:
+            # ring SP (ops/fa_h3.py:159-218): local queries, K/V chunks passed
+            # around the ring, chunk results merged through their LSEs
+            flops = 4.0 * s_local * s_local * state().world_size * self.head_dim * self.heads
+            o = ATTN_TIMER.record(lambda: ring_attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5,
+                                                         amax_out=amax_o), flops)
+            o = o.view(s_local, self.heads * self.head_dim)
+            global_amax_(amax_o, self.out_proj)
+        elif gather_kv:
             # the reference's production SP (model/dit.py:200-248): local
             # queries over the gathered keys/values of all ranks, all heads
             k, v = all_gather_kv(q3[:, 1], q3[:, 2])

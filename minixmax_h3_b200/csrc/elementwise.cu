@@ -217,6 +217,63 @@ __global__ void __launch_bounds__(256) gate_residual_kernel(__nv_bfloat16* __res
 
 }  // namespace
 
+// Merge of two attention results over disjoint key sets through their row
+// log-sum-exps, in fp32 (ops/fa_h3.py:141-156):
+//   o   <- o - sigmoid(l_b - l_o) * (o - o_b)
+//   l_o <- l_o - logsigmoid(l_o - l_b) = max(l_o, l_b) + log1p(exp(-|l_o - l_b|))
+// first: o <- o_b, l_o <- l_b.  One warp per (token, head) row of 128; acc is
+// fp32 and blk / out bf16, all token-major [s, heads, 128]; lse [heads, s].
+// With out given (the last merge) the result goes to out as bf16, with its
+// max |value| into amax_out, and acc is not written back.
+__global__ void __launch_bounds__(256) merge_lse_kernel(float* __restrict__ acc, float* __restrict__ acc_lse,
+                                                        const __nv_bfloat16* __restrict__ blk,
+                                                        const float* __restrict__ blk_lse, int64_t s,
+                                                        int64_t heads, int first,
+                                                        __nv_bfloat16* __restrict__ out,
+                                                        float* __restrict__ amax_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = s * heads;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  float amax = 0.0f;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int64_t t = r / heads;
+    const int64_t li = (r - t * heads) * s + t;
+    const uint2 bv = *reinterpret_cast<const uint2*>(blk + r * 128 + lane * 4);
+    const float b[4] = {bf16lo_to_f32(bv.x), bf16hi_to_f32(bv.x), bf16lo_to_f32(bv.y), bf16hi_to_f32(bv.y)};
+    float4* ap = reinterpret_cast<float4*>(acc + r * 128 + lane * 4);
+    const float lb = blk_lse[li];
+    float o[4];
+    float l_new;
+    if (first) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = b[e];
+      l_new = lb;
+    } else {
+      const float4 av = *ap;
+      const float a[4] = {av.x, av.y, av.z, av.w};
+      const float lo = acc_lse[li];
+      const float d = lo - lb;
+      const float w = __fdiv_rn(1.0f, 1.0f + expf(d));  // sigmoid(lb - lo)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = a[e] - w * (a[e] - b[e]);
+      l_new = fmaxf(lo, lb) + log1pf(expf(-fabsf(d)));
+    }
+    if (lane == 0) acc_lse[li] = l_new;
+    if (out == nullptr) {
+      *ap = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+      const uint2 ov = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      *reinterpret_cast<uint2*>(out + r * 128 + lane * 4) = ov;
+      amax = fmax3(amax, fmaxf(fabsf(bf16lo_to_f32(ov.x)), fabsf(bf16hi_to_f32(ov.x))),
+                   fmaxf(fabsf(bf16lo_to_f32(ov.y)), fabsf(bf16hi_to_f32(ov.y))));
+    }
+  }
+  if (amax_out != nullptr) {
+    amax = warp_max(amax);
+    if (lane == 0 && amax > 0.0f) atomicMax(reinterpret_cast<unsigned int*>(amax_out), __float_as_uint(amax));
+  }
+}
+
 extern "C" int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, int64_t seq_stride,
                                    int64_t head_stride, const void* q_weight, const void* k_weight, float eps,
                                    const float* pos, int64_t pos_offset, const float* inv_freq, int n_t, int n_h,
@@ -282,5 +339,20 @@ extern "C" int h3b_gate_residual(void* x, const void* y, int64_t m, int64_t hidd
   gate_residual_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), m, hidden, ld,
       static_cast<const __nv_bfloat16*>(gate), tab_ld, row_sel);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_attention_merge_lse(float* acc, float* acc_lse, const void* blk, const float* blk_lse, int64_t s,
+                                       int64_t heads, int first, void* out, float* amax_out, h3b_stream_t stream) {
+  if (acc == nullptr || acc_lse == nullptr || blk == nullptr || blk_lse == nullptr) return H3B_ERR_ARG;
+  if (s < 0 || heads <= 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(acc) || !h3b::aligned16(blk) || (out != nullptr && !h3b::aligned16(out))) return H3B_ERR_ALIGN;
+  if (s == 0) return H3B_OK;
+  int64_t blocks = (s * heads + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(h3b::num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  merge_lse_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      acc, acc_lse, static_cast<const __nv_bfloat16*>(blk), blk_lse, s, heads, first,
+      static_cast<__nv_bfloat16*>(out), amax_out);
   return h3b::launch_status();
 }

@@ -271,6 +271,29 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optio
     return out
 
 
+def attention_merge_lse(acc: torch.Tensor, acc_lse: torch.Tensor, blk: torch.Tensor, blk_lse: torch.Tensor, *,
+                        first: bool, out: Optional[torch.Tensor] = None,
+                        amax_out: Optional[torch.Tensor] = None) -> None:
+    """Fold one key chunk's attention result (blk bf16 [S, H, 128], blk_lse
+    [H, S]) into the running fp32 result acc / acc_lse (ops/fa_h3.py:141-156);
+    first=True initialises them.  With out (bf16 [S, H, 128]) given, the merged
+    rows go there (and max |out| into amax_out) instead of acc."""
+    _cuda(acc, acc_lse, blk, blk_lse, out, amax_out)
+    s, heads, d = blk.shape
+    if d != 128 or acc.shape != blk.shape or acc_lse.shape != (heads, s) or blk_lse.shape != (heads, s):
+        raise ValueError("attention_merge_lse: acc/blk [S, H, 128], lse [H, S]")
+    if acc.dtype != torch.float32 or blk.dtype != torch.bfloat16 or acc_lse.dtype != torch.float32 \
+            or blk_lse.dtype != torch.float32:
+        raise ValueError("attention_merge_lse: acc fp32, blk bf16, lse fp32")
+    tensors = (acc, acc_lse, blk, blk_lse) + ((out,) if out is not None else ())
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("attention_merge_lse: contiguous tensors only")
+    if out is not None and (out.shape != blk.shape or out.dtype != torch.bfloat16):
+        raise ValueError("attention_merge_lse: out bf16 [S, H, 128]")
+    call("h3b_attention_merge_lse", acc.data_ptr(), acc_lse.data_ptr(), blk.data_ptr(), blk_lse.data_ptr(), s, heads,
+         1 if first else 0, _ptr(out), _ptr(amax_out), _stream(blk))
+
+
 def attention_head2seq(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o_ptrs: Sequence[int], *,
                        s_local: int, head0: int, total_heads: int, scale: Optional[float] = None,
                        amax_out: Optional[torch.Tensor] = None) -> None:

@@ -28,15 +28,17 @@ from typing import Optional, Sequence
 import torch
 import torch.distributed as tdist
 
+from . import ops
 from ._lib import call
 from .dist import is_distributed, state
 
 
 def transport() -> str:
-    """"p2p" (fused P2P stores, default), "nccl" or "allgather" (H3B_ULYSSES)."""
+    """"p2p" (fused P2P stores, default), "nccl", "allgather" or "ring"
+    (H3B_ULYSSES)."""
     t = os.environ.get("H3B_ULYSSES", "p2p")
-    if t not in ("p2p", "nccl", "allgather"):
-        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p, nccl or allgather")
+    if t not in ("p2p", "nccl", "allgather", "ring"):
+        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p, nccl, allgather or ring")
     return t
 
 
@@ -165,6 +167,59 @@ def all_gather_kv(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch
     out = torch.empty((st.world_size * kv.shape[0],) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
     tdist.all_gather_into_tensor(out, kv, group=st.group)
     return out[:, 0], out[:, 1]
+
+
+def _global_rank(group, r: int) -> int:
+    return r if group is None or group is tdist.group.WORLD else tdist.get_global_rank(group, r)
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
+                   out: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
+                   attention_fn=None, merge_fn=None) -> torch.Tensor:
+    """Ring sequence parallelism (ops/fa_h3.py:159-218, ring_attention_lse_bnsd):
+    this rank's queries q [S_local, H, D] attend to every rank's keys/values,
+    which travel around the ring (rank r sends to r+1 and receives from r-1)
+    one chunk per step while the chunk in hand is processed; the chunk results
+    are merged through their log-sum-exps in fp32 (ops.attention_merge_lse)
+    and the last merge writes out [S_local, H, D] bf16 (max |out| into
+    amax_out).  K and V travel as one [S_local, 2, H, D] buffer.
+
+    attention_fn(q, k, v, scale, out, lse) and merge_fn(acc, acc_lse, blk,
+    blk_lse, first=, out=, amax_out=) default to this package's kernels; they
+    are parameters so the ring logic can be exercised on CPU."""
+    s_l, heads, d = q.shape
+    scale = d ** -0.5 if scale is None else float(scale)
+    if out is None:
+        out = torch.empty(s_l, heads, d, dtype=torch.bfloat16, device=q.device)
+    if attention_fn is None:
+        def attention_fn(q_, k_, v_, sc, o_, lse_):
+            ops.attention(q_, k_, v_, scale=sc, out=o_, lse=lse_)
+    merge_fn = merge_fn or ops.attention_merge_lse
+    ws = state().world_size if is_distributed() else 1
+    rank = state().rank if is_distributed() else 0
+    group = state().group if is_distributed() else None
+    kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
+    recv = torch.empty_like(kv) if ws > 1 else None
+    acc = torch.empty(s_l, heads, d, dtype=torch.float32, device=q.device)
+    acc_lse = torch.empty(heads, s_l, dtype=torch.float32, device=q.device)
+    blk = torch.empty(s_l, heads, d, dtype=torch.bfloat16, device=q.device)
+    blk_lse = torch.empty(heads, s_l, dtype=torch.float32, device=q.device)
+    nxt, prv = _global_rank(group, (rank + 1) % ws), _global_rank(group, (rank + ws - 1) % ws)
+    reqs: list = []
+    for step in range(ws):
+        if step > 0:
+            for r in reqs:
+                r.wait()
+            kv, recv = recv, kv
+        reqs = []
+        if step + 1 < ws:
+            reqs = tdist.batch_isend_irecv([tdist.P2POp(tdist.isend, kv, nxt, group),
+                                            tdist.P2POp(tdist.irecv, recv, prv, group)])
+        attention_fn(q, kv[:, 0], kv[:, 1], scale, blk, blk_lse)
+        last = step == ws - 1
+        merge_fn(acc, acc_lse, blk, blk_lse, first=step == 0, out=out if last else None,
+                 amax_out=amax_out if last else None)
+    return out
 
 
 def split_range(seq_len: int) -> tuple[int, int]:

@@ -329,6 +329,32 @@ def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Opt
     return F.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=scale)
 
 
+def attention_lse_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None
+                       ) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o, lse) of non-causal attention in fp32, token-major q [Sq, H, D],
+    k/v [Skv, H, D]: o [Sq, H, D] and the natural-log row log-sum-exp
+    [H, Sq] — what the FA call with softmax_lse_flag returns in
+    ops/fa_h3.py:207-210."""
+    d = q.shape[-1]
+    scale = d ** -0.5 if scale is None else scale
+    logits = torch.einsum("shd,thd->hst", q.float(), k.float()) * scale
+    lse = torch.logsumexp(logits, dim=-1)
+    o = torch.einsum("hst,thd->shd", torch.softmax(logits, dim=-1), v.float())
+    return o, lse
+
+
+def merge_lse(acc_o: torch.Tensor, acc_lse: torch.Tensor, blk_o: torch.Tensor, blk_lse: torch.Tensor
+              ) -> tuple[torch.Tensor, torch.Tensor]:
+    """ops/fa_h3.py:141-156 (_merge_lse) for token-major o [S, H, D] and
+    lse [H, S]: o - sigmoid(l_b - l_o) * (o - o_b), l_o - logsigmoid(l_o - l_b),
+    in fp32."""
+    o, bo = acc_o.float(), blk_o.float()
+    lo, ln = acc_lse.float().t()[..., None], blk_lse.float().t()[..., None]  # [S, H, 1]
+    o = o - torch.sigmoid(ln - lo) * (o - bo)
+    lo = lo - F.logsigmoid(lo - ln)
+    return o, lo[..., 0].t().contiguous()
+
+
 # ----------------------------------------------------------------------------- Ulysses
 
 

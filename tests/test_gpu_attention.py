@@ -147,3 +147,61 @@ def test_rmsnorm_modulate_and_gate(cuda):
     ops.gate_residual(xd, y.to(cuda), gate.to(cuda))
     want_x = O.mod_gate(x.clone(), gate[None], y, [(0, m, 0)])
     assert_close_bf16(xd, want_x, max_abs=1e-2)
+
+
+# ---------------------------------------------------------------- LSE merge (ring SP)
+
+def test_merge_lse_kernel_matches_reference_formula(cuda):
+    """h3b_attention_merge_lse vs ops/fa_h3.py:141-156 restated in fp32."""
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(11)
+    s, heads = 333, 3
+    acc = torch.randn(s, heads, 128, generator=g)
+    blk = torch.randn(s, heads, 128, generator=g).to(torch.bfloat16)
+    acc_lse = torch.randn(heads, s, generator=g) * 4
+    blk_lse = torch.randn(heads, s, generator=g) * 4
+    a, al = acc.to(cuda), acc_lse.to(cuda)
+    ops.attention_merge_lse(a, al, blk.to(cuda), blk_lse.to(cuda), first=False)
+    want_o, want_l = O.merge_lse(acc, acc_lse, blk, blk_lse)
+    assert torch.allclose(a.cpu(), want_o, atol=1e-5, rtol=1e-5)
+    assert torch.allclose(al.cpu(), want_l, atol=1e-5, rtol=1e-6)
+    # final merge: bf16 out and its |max|, acc untouched
+    a2, al2 = acc.to(cuda), acc_lse.to(cuda)
+    out = torch.empty(s, heads, 128, dtype=torch.bfloat16, device=cuda)
+    amax = torch.zeros(1, device=cuda)
+    ops.attention_merge_lse(a2, al2, blk.to(cuda), blk_lse.to(cuda), first=False, out=out, amax_out=amax)
+    assert torch.equal(a2.cpu(), acc)
+    assert torch.allclose(out.float().cpu(), want_o, atol=2e-2, rtol=1e-2)
+    assert amax.item() == out.float().abs().max().item()
+    # first: plain copy
+    ops.attention_merge_lse(a, al, blk.to(cuda), blk_lse.to(cuda), first=True)
+    assert torch.equal(a.cpu(), blk.float()) and torch.equal(al.cpu(), blk_lse)
+
+
+@pytest.mark.parametrize("chunks", [2, 3])
+def test_chunked_attention_with_lse_merge(cuda, chunks):
+    """Attention over K/V split into chunks, merged through the LSEs (the ring
+    step, here on one GPU), against attention over the whole K/V."""
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(chunks)
+    s_q, s_kv, heads = 300, 384 * chunks, 2
+    q = torch.randn(s_q, heads, 128, generator=g).to(torch.bfloat16).to(cuda)
+    k = torch.randn(s_kv, heads, 128, generator=g).to(torch.bfloat16).to(cuda)
+    v = torch.randn(s_kv, heads, 128, generator=g).to(torch.bfloat16).to(cuda)
+    acc = torch.empty(s_q, heads, 128, device=cuda)
+    acc_lse = torch.empty(heads, s_q, device=cuda)
+    blk = torch.empty(s_q, heads, 128, dtype=torch.bfloat16, device=cuda)
+    blk_lse = torch.empty(heads, s_q, device=cuda)
+    out = torch.empty_like(blk)
+    c = s_kv // chunks
+    for i in range(chunks):
+        ops.attention(q, k[i * c:(i + 1) * c], v[i * c:(i + 1) * c], out=blk, lse=blk_lse)
+        ops.attention_merge_lse(acc, acc_lse, blk, blk_lse, first=i == 0, out=out if i == chunks - 1 else None)
+    full_lse = torch.empty(heads, s_q, device=cuda)
+    full = ops.attention(q, k, v, lse=full_lse)
+    assert torch.allclose(acc_lse, full_lse, atol=1e-4, rtol=1e-5)
+    assert_close_bf16(out, _ref_tokens_major(q.cpu(), k.cpu(), v.cpu()))
+    g_, w_ = out.float().reshape(-1), full.float().reshape(-1)
+    assert torch.nn.functional.cosine_similarity(g_, w_, dim=0).item() > 0.9999

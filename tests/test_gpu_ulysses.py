@@ -8,7 +8,14 @@ result must match the same block run on one GPU.  With INT8 (per-token
 activation scales) every token sees identical arithmetic on both paths, so the
 match is exact.  With NVFP4 the activation global scales are max-reduced
 across ranks (block.global_amax_), so the sharded run quantises exactly as
-the single-GPU run and the match is exact too."""
+the single-GPU run and the match is exact too.  The ring scheme ("ring",
+ops/fa_h3.py:159-218) merges per-chunk attention results through their
+log-sum-exps, so its attention output differs from the single-GPU one at bf16
+rounding level; the out-projection's activation quantiser (4-bit NVFP4 codes,
+8-bit INT8) turns a few of those differences into one-code flips, so the
+block output is checked by cosine >= 0.9999 over the whole tensor and a max
+relative error <= 0.1 (a wrong chunk or merge is O(1)).  Measured on 2 B200s
+for NVFP4 / GELU: cosine 0.9999989, max relative error 0.043."""
 from __future__ import annotations
 
 import os
@@ -83,6 +90,8 @@ def _worker(rank: int, ws: int, port: int, fmt: str, transport: str, mlp_act: st
     ("nvfp4", "nccl", "gelu"),
     ("int8_tensorwise", "allgather", "gelu"),
     ("nvfp4", "allgather", "swiglu"),
+    ("nvfp4", "ring", "gelu"),
+    ("int8_tensorwise", "ring", "swiglu"),
 ])
 def test_ulysses_block_matches_single_gpu(fmt, transport, mlp_act):
     if torch.cuda.device_count() < 2:
@@ -101,4 +110,7 @@ def test_ulysses_block_matches_single_gpu(fmt, transport, mlp_act):
             if p.is_alive():
                 p.kill()
     assert status == "ok", exact
-    assert exact, (err, cos)
+    if transport == "ring":
+        assert err <= 0.1 and cos >= 0.9999, (err, cos)
+    else:
+        assert exact, (err, cos)

@@ -1,7 +1,9 @@
-"""CPU, world_size 2/4 over gloo: the Ulysses exchanges and the K/V all-gather
-of minixmax_h3_b200.ulysses reproduce the reference's layouts
-(ops/ulysses.py, runtime/dist.py) bit-for-bit, and a rank that dies is
-reported by the others as an error."""
+"""CPU, world_size 2/3/4 over gloo: the Ulysses exchanges and the K/V
+all-gather of minixmax_h3_b200.ulysses reproduce the reference's layouts
+(ops/ulysses.py, runtime/dist.py) bit-for-bit, the ring scheme
+(ops/fa_h3.py:141-218) with the oracle's attention and LSE merge plugged in
+matches attention over every rank's keys, and a rank that dies is reported by
+the others as an error."""
 from __future__ import annotations
 
 import os
@@ -56,6 +58,30 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
             segs = [(0, 5, 1), (5, s, 0)]
             assert U.clip_mod_segments(segs, s0, s1) == O.clip_mod_segments(segs, s0, s1)
             results.put((rank, "ok"))
+        elif mode == "ring":
+            g = torch.Generator().manual_seed(7)
+            qf, kf, vf = (torch.randn(s, h, 16, generator=g).to(torch.bfloat16) for _ in range(3))
+
+            def attn(q_, k_, v_, sc, o_, lse_):
+                o, lse = O.attention_lse_fp32(q_, k_, v_, sc)
+                o_.copy_(o.to(torch.bfloat16))
+                lse_.copy_(lse)
+
+            def merge(acc, acc_lse, blk, blk_lse, first, out=None, amax_out=None):
+                if first:
+                    acc.copy_(blk.float())
+                    acc_lse.copy_(blk_lse)
+                else:
+                    o, lse = O.merge_lse(acc, acc_lse, blk, blk_lse)
+                    acc.copy_(o)
+                    acc_lse.copy_(lse)
+                if out is not None:
+                    out.copy_(acc.to(torch.bfloat16))
+
+            got = U.ring_attention(qf[s0:s1], kf[s0:s1], vf[s0:s1], attention_fn=attn, merge_fn=merge)
+            want, _ = O.attention_lse_fp32(qf[s0:s1], kf, vf)
+            err = (got.float() - want).abs().max().item()
+            results.put((rank, "ok" if err < 1e-2 else f"ring err {err}"))
         elif mode == "dead_peer":
             U.all_to_all_heads(local, gather_seq=True)  # a healthy step: connections are up
             if rank == ws - 1:
@@ -96,6 +122,12 @@ def _run(ws: int, mode: str, timeout: float = 120.0) -> dict:
 @pytest.mark.parametrize("ws", [2, 4])
 def test_ulysses_exchanges_match_reference_layout(ws):
     res = _run(ws, "exchange")
+    assert res == {r: "ok" for r in range(ws)}, res
+
+
+@pytest.mark.parametrize("ws", [2, 3])
+def test_ring_attention_matches_full_attention(ws):
+    res = _run(ws, "ring")
     assert res == {r: "ok" for r in range(ws)}, res
 
 
