@@ -231,6 +231,20 @@ H3B_API int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t hidd
                                  float eps, float* amax_out, h3b_stream_t stream);
 
 /*
+ * h3b_rmsnorm_modulate followed by the INT8 row quantiser of the QKV / fc1
+ * input — h3b_quant_i8_rows (convrot_group 0) or h3b_quant_i8_rows_convrot
+ * (convrot_group 256) applied to h — in one pass, without writing h: the
+ * norm + _mod_scale_shift of model/dit.py:433-438 feeding
+ * int8_convrot_linear (ops/int8_convrot.py:114-157).  q: [m, hidden] int8
+ * (row stride hidden, 8-byte aligned), q_scale: [m] fp32.  Same bits as the
+ * two-kernel sequence.  hidden % 256 == 0 with ConvRot.
+ */
+H3B_API int h3b_rmsnorm_modulate_quant_i8(const void* x, int64_t m, int64_t hidden, int64_t ld, const void* w,
+                                          const void* shift, const void* scale, int64_t tab_ld,
+                                          const int32_t* row_sel, float eps, int64_t convrot_group, int8_t* q,
+                                          float* q_scale, h3b_stream_t stream);
+
+/*
  * x[r,:] += y[r,:] * gate_r  (bf16, in place), the _mod_gate of
  * model/dit.py:338-341; gate_r = gate + row_sel[r]*tab_ld, rows with
  * row_sel < 0 unchanged.

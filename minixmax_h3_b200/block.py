@@ -28,7 +28,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .dist import is_distributed, state
-from .modules import Linear, Ops, QuantLinear, RMSNorm
+from .modules import Linear, Ops, QuantizedRows, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
 from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer,
                       phase_barrier, ring_attention, split_range, transport)
@@ -315,12 +315,25 @@ class DiTBlock(nn.Module):
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(t_emb)
         sel = self._row_sel(mod_segments, x.shape[0], x.device)
         amax = torch.zeros(2, dtype=torch.float32, device=x.device)
-        h = ops.rmsnorm_modulate(x, self.norm1.weight, shift_msa, scale_msa, self.norm1.eps, row_sel=sel,
-                                 amax_out=amax[0:1])
-        self.attn(h, rope_freqs, amax_h=amax[0:1], resid=x, gate=gate_msa, row_sel=sel)
-        h = ops.rmsnorm_modulate(x, self.norm2.weight, shift_mlp, scale_mlp, self.norm2.eps, row_sel=sel,
-                                 amax_out=amax[1:2], out=h)
-        self.mlp(h, amax_h=amax[1:2], resid=x, gate=gate_mlp, row_sel=sel)
+        h = None
+        for i, (norm, shift, scale, gate, sub, ql) in enumerate((
+                (self.norm1, shift_msa, scale_msa, gate_msa, self.attn, self.attn.qkv_proj),
+                (self.norm2, shift_mlp, scale_mlp, gate_mlp, self.mlp, self.mlp.fc1))):
+            if ql.quant_format == "int8_tensorwise":
+                # norm + modulate + (ConvRot) + row quantisation in one kernel
+                group = ql.group_size if ql.convrot else 0
+                q, xs = ops.rmsnorm_modulate_quant_i8(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
+                                                      convrot_group=group,
+                                                      q_out=h.q if isinstance(h, QuantizedRows) else None,
+                                                      scale_out=h.scale if isinstance(h, QuantizedRows) else None)
+                h = QuantizedRows(q, xs, group)
+            else:
+                h = ops.rmsnorm_modulate(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
+                                         amax_out=amax[i:i + 1], out=h if isinstance(h, torch.Tensor) else None)
+            if i == 0:
+                sub(h, rope_freqs, amax_h=amax[0:1], resid=x, gate=gate, row_sel=sel)
+            else:
+                sub(h, amax_h=amax[1:2], resid=x, gate=gate, row_sel=sel)
         return x
 
 

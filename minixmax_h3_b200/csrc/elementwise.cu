@@ -12,6 +12,7 @@
 //  * gate_residual: x += y*gate (model/dit.py:338-341).
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
+#include "h3b_rownorm.cuh"
 
 namespace {
 
@@ -113,67 +114,19 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float amax = 0.0f;
   for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
-  const __nv_bfloat16* xr = x + row * ld;
-  uint4 v[MAXV];
-  float ss = 0.0f;
+    const int sel = row_sel != nullptr ? row_sel[row] : 0;
+    const bool modulate = sel >= 0;
+    const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
+    const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
+    uint4 v[MAXV];
+    amax = fmaxf(amax, h3b::rmsnorm_modulate_row<MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r,
+                                                       modulate, red, v));
+    __nv_bfloat16* hr = h + row * ld;
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int vi = threadIdx.x + i * 256;
-    if (vi < nvec) {
-      v[i] = *reinterpret_cast<const uint4*>(xr + vi * 8);
-      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = bf16lo_to_f32(u[e]), b = bf16hi_to_f32(u[e]);
-        ss += a * a + b * b;
-      }
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) *reinterpret_cast<uint4*>(hr + vi * 8) = v[i];
     }
-  }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < 8 ? red[lane] : 0.0f;
-    t = warp_sum(t);
-    if (lane == 0) red[32] = t;
-  }
-  __syncthreads();
-  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(red[32], static_cast<float>(hidden)) + eps));
-  __syncthreads();  // red[] is reused by the next row
-  __nv_bfloat16* hr = h + row * ld;
-  const int sel = row_sel != nullptr ? row_sel[row] : 0;
-  const bool modulate = sel >= 0;
-  const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
-  const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int vi = threadIdx.x + i * 256;
-    if (vi < nvec) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
-      const uint4 sh = *reinterpret_cast<const uint4*>(shift_r + vi * 8);
-      const uint4 sc = *reinterpret_cast<const uint4*>(scale_r + vi * 8);
-      const uint32_t xu[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
-      const uint32_t shu[4] = {sh.x, sh.y, sh.z, sh.w};
-      const uint32_t scu[4] = {sc.x, sc.y, sc.z, sc.w};
-      uint32_t outw[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // both bf16 halves of the 32-bit word together: one packed rounding per step
-        const float2 nrm = bf16r2(__fmul_rn(__fmul_rn(bf16lo_to_f32(xu[e]), rstd), bf16lo_to_f32(wu[e])),
-                                  __fmul_rn(__fmul_rn(bf16hi_to_f32(xu[e]), rstd), bf16hi_to_f32(wu[e])));
-        float2 mod = nrm;
-        if (modulate) {
-          const float2 s1 = bf16r2(1.0f + bf16lo_to_f32(scu[e]), 1.0f + bf16hi_to_f32(scu[e]));
-          const float2 t = bf16r2(nrm.x * s1.x, nrm.y * s1.y);
-          mod = bf16r2(t.x + bf16lo_to_f32(shu[e]), t.y + bf16hi_to_f32(shu[e]));
-        }
-        amax = fmax3(amax, fabsf(mod.x), fabsf(mod.y));
-        outw[e] = pack_bf16x2(mod.x, mod.y);
-      }
-      *reinterpret_cast<uint4*>(hr + vi * 8) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
-    }
-  }
   }
   if (amax_out != nullptr) {
     amax = warp_max(amax);

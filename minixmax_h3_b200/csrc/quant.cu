@@ -12,6 +12,7 @@
 
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
+#include "h3b_rownorm.cuh"
 
 H3B_DECLARE_STATUS();
 H3B_REGISTER_STATUS_READER(quant);
@@ -421,6 +422,81 @@ int launch_quant_i8(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q,
   return h3b::launch_status();
 }
 
+// RMSNorm + adaLN modulate + INT8 row quantisation (ROT: with the ConvRot
+// rotation of every 256-column group in between) — the values of
+// rmsnorm_modulate followed by quant_i8_rows / quant_i8_rows_convrot on its
+// bf16 output (int8_convrot.py:114-157 on the output of dit.py:433-434),
+// without writing that output: the row stays in registers.  In the row
+// layout of rmsnorm_modulate_row, warp w's chunk i is exactly ConvRot group
+// w + 8 i with element 8 lane + e in lane `lane`, the order
+// hadamard256_warp rotates, so ROT needs no data movement.
+template <int MAXV, bool ROT>
+__global__ void __launch_bounds__(256) rmsnorm_modulate_quant_i8_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t m, int64_t hidden, int64_t ld, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale, int64_t tab_ld,
+    const int32_t* __restrict__ row_sel, float eps, int8_t* __restrict__ q, float* __restrict__ q_scale) {
+  __shared__ float red[33];
+  const int nvec = static_cast<int>(hidden >> 3);
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+    const int sel = row_sel != nullptr ? row_sel[row] : 0;
+    const bool modulate = sel >= 0;
+    const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
+    const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
+    uint4 v[MAXV];
+    float amax = h3b::rmsnorm_modulate_row<MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r, modulate,
+                                                 red, v);
+    float f[MAXV][8];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {  // warp-uniform when ROT (hidden % 256 == 0)
+        unpack8<__nv_bfloat16>(v[i], f[i]);
+        if constexpr (ROT) {
+          double d[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) d[e] = static_cast<double>(f[i][e]);
+          hadamard256_warp(d);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[i][e] = __bfloat162float(f64_round<__nv_bfloat16>(d[e] * 0.0625));
+        }
+      }
+    }
+    if constexpr (ROT) {
+      amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        if (threadIdx.x + i * 256 < nvec) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[i][e]));
+        }
+      }
+    }
+    amax = block_max<256>(amax, red);
+    amax = fmaxf(amax, 1e-12f);
+    const float s = __fdiv_rn(amax, 127.0f);
+    const bool fast = rcp_div_ok(s);
+    const float y = __frcp_rn(s);
+    int8_t* qr = q + row * hidden;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float fj = f[i][j];
+          float r = rintf((fast && fabsf(fj) >= 0x1p-90f) ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
+          r = fminf(fmaxf(r, -128.0f), 127.0f);
+          const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
+          packed[j >> 2] |= b << ((j & 3) * 8);
+        }
+        *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * 8) = make_uint2(packed[0], packed[1]);
+      }
+    }
+    if (threadIdx.x == 0) q_scale[row] = s;
+  }
+}
+
 }  // namespace
 
 extern "C" int h3b_quant_i8_rows(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int8_t* q,
@@ -496,5 +572,48 @@ extern "C" int h3b_nvfp4_swap_nibbles(const uint8_t* src, uint8_t* dst, int64_t 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   swap_nibbles_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
                                                                       reinterpret_cast<uint4*>(dst), nvec);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_rmsnorm_modulate_quant_i8(const void* x, int64_t m, int64_t hidden, int64_t ld, const void* w,
+                                             const void* shift, const void* scale, int64_t tab_ld,
+                                             const int32_t* row_sel, float eps, int64_t convrot_group, int8_t* q,
+                                             float* q_scale, h3b_stream_t stream) {
+  if (x == nullptr || w == nullptr || shift == nullptr || scale == nullptr || q == nullptr || q_scale == nullptr)
+    return H3B_ERR_ARG;
+  if (m < 0 || hidden <= 0 || (hidden % 8) != 0 || ld < hidden || (ld % 8) != 0 || m > 0x7fffffff)
+    return H3B_ERR_SHAPE;
+  if (convrot_group != 0 && (convrot_group != 256 || (hidden % 256) != 0)) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || !h3b::aligned16(w) || !h3b::aligned16(shift) || !h3b::aligned16(scale) ||
+      (reinterpret_cast<uintptr_t>(q) & 7u) != 0 || tab_ld < 0 || (tab_ld % 8) != 0)
+    return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  const auto* sh = static_cast<const __nv_bfloat16*>(shift);
+  const auto* sc = static_cast<const __nv_bfloat16*>(scale);
+  const int64_t nvec = hidden / 8;
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * 8;
+  if (blocks > m) blocks = m;
+  const unsigned g = static_cast<unsigned>(blocks);
+  const bool rot = convrot_group == 256;
+  if (nvec <= 256 * 2) {
+    if (rot)
+      rmsnorm_modulate_quant_i8_kernel<2, true><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
+                                                                   eps, q, q_scale);
+    else
+      rmsnorm_modulate_quant_i8_kernel<2, false><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
+                                                                    eps, q, q_scale);
+  } else if (nvec <= 256 * 8) {
+    if (rot)
+      rmsnorm_modulate_quant_i8_kernel<8, true><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
+                                                                   eps, q, q_scale);
+    else
+      rmsnorm_modulate_quant_i8_kernel<8, false><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
+                                                                    eps, q, q_scale);
+  } else {
+    return H3B_ERR_SHAPE;
+  }
   return h3b::launch_status();
 }

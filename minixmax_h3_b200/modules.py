@@ -10,6 +10,7 @@ per-tensor scale).  Compute goes to libh3b.so; there is no CPU path.
 from __future__ import annotations
 
 import json
+from dataclasses import dataclass
 from typing import Any, Optional
 
 import torch
@@ -62,6 +63,26 @@ class Linear(nn.Module):
         w = self.weight.to(dtype=x.dtype, device=x.device)
         b = self.bias.to(dtype=x.dtype, device=x.device) if self.bias is not None else None
         return F.linear(x, w, b)
+
+
+@dataclass
+class QuantizedRows:
+    """An activation already quantised for an INT8 QuantLinear: codes
+    q [m, K] int8 and per-row scales [m] fp32, rotated by ConvRot before
+    quantisation when convrot_group is 256 — e.g. from
+    ops.rmsnorm_modulate_quant_i8.  Accepted by the INT8 forward paths in
+    place of the bf16 input."""
+    q: torch.Tensor
+    scale: torch.Tensor
+    convrot_group: int = 0
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.q.shape
+
+    @property
+    def device(self) -> torch.device:
+        return self.q.device
 
 
 class QuantLinear(nn.Module):
@@ -184,7 +205,15 @@ class QuantLinear(nn.Module):
         self._row_perm = perm
         self._inv_perm = torch.argsort(perm)
 
-    def _bias(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+    def _quant_i8_input(self, x) -> tuple[torch.Tensor, torch.Tensor]:
+        group = self.group_size if self.convrot else 0
+        if isinstance(x, QuantizedRows):
+            if x.convrot_group != group:
+                raise ValueError(f"input quantised with ConvRot group {x.convrot_group}, layer expects {group}")
+            return x.q, x.scale
+        return ops.quant_i8_rows(x, convrot_group=group)
+
+    def _bias(self, x) -> Optional[torch.Tensor]:
         return None if self.bias is None or self.bias.numel() == 0 else self.bias.to(torch.bfloat16)
 
     def forward_fused(self, x: torch.Tensor, *, amax: Optional[torch.Tensor] = None, epilogue: int = EPI_STORE,
@@ -196,11 +225,13 @@ class QuantLinear(nn.Module):
         amax: precomputed max|x| (fp32 device scalar) for the NVFP4 global
         scale, e.g. from the producing kernel; computed here when None."""
         if self.quant_format == "int8_tensorwise":
-            q, xs = ops.quant_i8_rows(x, convrot_group=self.group_size if self.convrot else 0)
+            q, xs = self._quant_i8_input(x)
             return ops.gemm_i8(q, xs, self.weight_i8, self.weight_scale, self._bias(x), epilogue=epilogue,
                                resid=resid, gate=gate, row_sel=row_sel, amax_out=amax_out, out=out)
         if self.quant_format == "nvfp4":
             self.prepare_cube()
+            if isinstance(x, QuantizedRows):
+                raise TypeError("an NVFP4 layer needs the bf16 input, not INT8 QuantizedRows")
             a = ops.quant_nvfp4(x, amax_t=amax)
             return ops.gemm_nvfp4(a, self._w_nvfp4, self._bias(x), epilogue=epilogue, resid=resid, gate=gate,
                                   row_sel=row_sel, amax_out=amax_out, out=out)
@@ -212,11 +243,13 @@ class QuantLinear(nn.Module):
         owner's receive buffer (ops.gemm_*_seq2head): the projection and the
         seq->head Ulysses exchange in one kernel."""
         if self.quant_format == "int8_tensorwise":
-            q, xs = ops.quant_i8_rows(x, convrot_group=self.group_size if self.convrot else 0)
+            q, xs = self._quant_i8_input(x)
             ops.gemm_i8_seq2head(q, xs, self.weight_i8, self.weight_scale, self._bias(x), recv_ptrs, rank, heads)
             return
         if self.quant_format == "nvfp4":
             self.prepare_cube()
+            if isinstance(x, QuantizedRows):
+                raise TypeError("an NVFP4 layer needs the bf16 input, not INT8 QuantizedRows")
             a = ops.quant_nvfp4(x, amax_t=amax)
             ops.gemm_nvfp4_seq2head(a, self._w_nvfp4, self._bias(x), recv_ptrs, rank, heads)
             return

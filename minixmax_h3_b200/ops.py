@@ -349,6 +349,29 @@ def rmsnorm_modulate(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor,
     return out
 
 
+def rmsnorm_modulate_quant_i8(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                              eps: float, row_sel: Optional[torch.Tensor] = None, convrot_group: int = 0,
+                              q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None
+                              ) -> tuple[torch.Tensor, torch.Tensor]:
+    """rmsnorm_modulate(x, ...) followed by quant_i8_rows(h, convrot_group)
+    in one kernel (h is never written): returns (q [m, hidden] int8,
+    per-row scale [m] fp32), the same bits as the two calls."""
+    _cuda(x, weight, shift, scale, row_sel, q_out, scale_out)
+    x2, m, hidden, ld = _rows(x)
+    if shift.stride() != scale.stride():
+        raise ValueError("shift and scale tables must share strides")
+    if convrot_group not in (0, 256):
+        raise NotImplementedError(f"ConvRot group size {convrot_group}: this build rotates 256-column groups")
+    q = q_out if q_out is not None else torch.empty((m, hidden), dtype=torch.int8, device=x.device)
+    xs = scale_out if scale_out is not None else torch.empty(m, dtype=torch.float32, device=x.device)
+    if q.shape != (m, hidden) or not q.is_contiguous() or xs.numel() != m:
+        raise ValueError("rmsnorm_modulate_quant_i8: q [m, hidden] contiguous, scale [m]")
+    call("h3b_rmsnorm_modulate_quant_i8", x2.data_ptr(), m, hidden, ld, weight.data_ptr(), shift.data_ptr(),
+         scale.data_ptr(), _gate_ld(shift), _ptr(row_sel), eps, convrot_group, q.data_ptr(), xs.data_ptr(),
+         _stream(x))
+    return q, xs
+
+
 def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
                   row_sel: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x += y * gate[row_sel] in place (bf16)."""

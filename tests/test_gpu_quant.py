@@ -179,3 +179,29 @@ def test_convrot_quantlinear(cuda):
                                         weight_scale=emu.ws, device=cuda)
     y = ql(x.to(cuda))
     assert torch.equal(y.cpu(), emu(x))
+
+
+# ------------------------------------------------- fused norm + modulate + INT8
+
+@pytest.mark.parametrize("hidden", [512, 3072, 12288])
+@pytest.mark.parametrize("group", [0, 256])
+def test_rmsnorm_modulate_quant_i8_matches_two_kernels(cuda, hidden, group):
+    """One kernel == rmsnorm_modulate then quant_i8_rows(_convrot), bit for
+    bit, including rows outside every modulation segment (row_sel -1)."""
+    from minixmax_h3_b200 import ops
+
+    g = torch.Generator().manual_seed(hidden + group)
+    m = 300
+    x = (torch.randn(m, hidden, generator=g) * 3).to(torch.bfloat16).to(cuda)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16).to(cuda)
+    tab = (0.2 * torch.randn(3, 2 * hidden, generator=g)).to(torch.bfloat16).to(cuda)
+    shift, scale = tab[:, :hidden], tab[:, hidden:]
+    sel = torch.randint(-1, 3, (m,), generator=g, dtype=torch.int32).to(cuda)
+    q, xs = ops.rmsnorm_modulate_quant_i8(x, w, shift, scale, 1e-6, row_sel=sel, convrot_group=group)
+    h = ops.rmsnorm_modulate(x, w, shift, scale, 1e-6, row_sel=sel)
+    q_ref, xs_ref = ops.quant_i8_rows(h, convrot_group=group)
+    assert torch.equal(q, q_ref) and torch.equal(xs, xs_ref)
+    # and against the oracle's restatement of the same chain
+    rot = O.rotate_activation_exact(h.cpu(), 256) if group else h.cpu()
+    q_o, xs_o = O.dynamic_quant_rows(rot)
+    assert torch.equal(q.cpu(), q_o) and torch.equal(xs.cpu(), xs_o)
