@@ -318,6 +318,30 @@ H3B_API int h3b_attention_fwd_head2seq(const void* q, const void* k, const void*
 H3B_API int h3b_attention_merge_lse(float* acc, float* acc_lse, const void* blk, const float* blk_lse, int64_t s,
                                     int64_t heads, int first, void* out, float* amax_out, h3b_stream_t stream);
 
+/*
+ * Allocation-free variant of the NVFP4 projection input: the results of
+ * h3b_rmsnorm_modulate (x -> h, with the |h| max) followed by
+ * h3b_quant_nvfp4 (h -> codes, sf, gs_out), with h and the max kept in a
+ * fixed array of this library's device memory instead of two caller
+ * buffers.  No counterpart in the reference: it is for callers that may not
+ * allocate device memory while they run (a framework that owns the GPU's
+ * memory pool, or C/C++ code without a caching allocator, for which
+ * cudaMalloc/cudaFree would synchronise the device).  The caller passes x,
+ * the tables and the outputs, with the meanings of the two entry points
+ * above (hidden % 64 == 0).  Limit: m * ld * 2 <= 16 MiB (h is held with the
+ * row stride of x); larger calls return H3B_ERR_SHAPE and do nothing.  The
+ * array (16 MiB + 256 bytes) is resident on every GPU that loads the
+ * library until the process exits; all calls on a device share it, so calls
+ * that overlap on the GPU race.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.
+ */
+H3B_API int h3b_rmsnorm_modulate_quant_nvfp4_noalloc(const void* x, int64_t m, int64_t hidden, int64_t ld,
+                                                     const void* w, const void* shift, const void* scale,
+                                                     int64_t tab_ld, const int32_t* row_sel, float eps,
+                                                     uint8_t* codes, uint8_t* sf, float* gs_out, int hi_first,
+                                                     h3b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

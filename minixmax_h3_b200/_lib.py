@@ -44,6 +44,8 @@ SIGNATURES: dict[str, list] = {
     "h3b_gate_residual": [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr],
     "h3b_rmsnorm_modulate_quant_i8": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_f32, c_i64,
                                       c_ptr, c_ptr, c_ptr],
+    "h3b_rmsnorm_modulate_quant_nvfp4_noalloc": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
+                                                 c_f32, c_ptr, c_ptr, c_ptr, c_int, c_ptr],
     "h3b_attention_merge_lse": [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_int, c_ptr, c_ptr, c_ptr],
 }
 
