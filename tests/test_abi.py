@@ -44,6 +44,17 @@ def test_library_exports_every_symbol():
     ("h3b_attention_fwd", (16,) * 4 + (None, None, 1, 1, 1, 100, 128, 128, 128, 128, 128, 0.1, None), 2),
     ("h3b_rmsnorm_modulate", (16, 16, 4, 100, 100, 16, 16, 16, 0, None, 1e-6, None, None), 1),
     ("h3b_amax_bf16", (16, 7, 16, None), 1),
+    ("h3b_attention_merge_lse", (None, 16, 16, 16, 4, 1, 0, None, None, None), 8),                # null acc
+    ("h3b_attention_merge_lse", (16, 16, 16, 16, 4, 0, 0, None, None, None), 1),                  # heads 0
+    ("h3b_attention_merge_lse", (16, 16, 24, 16, 4, 1, 0, None, None, None), 2),                  # blk unaligned
+    ("h3b_rmsnorm_modulate_quant_i8", (16, 4, 3072, 3072, 16, 16, 16, 0, None, 1e-6, 128, 16, 16, None), 1),
+    ("h3b_rmsnorm_modulate_quant_i8", (16, 4, 1000, 1000, 16, 16, 16, 0, None, 1e-6, 256, 16, 16, None), 1),
+    ("h3b_rmsnorm_modulate_quant_i8", (16, 4, 3072, 3072, 16, 16, 16, 0, None, 1e-6, 0, None, 16, None), 8),
+    # allocation-free NVFP4 input: rows beyond its 16 MiB array, and hidden % 64
+    ("h3b_rmsnorm_modulate_quant_nvfp4_noalloc", (16, 8193, 1024, 1024, 16, 16, 16, 0, None, 1e-6, 16, 16, 16, 1,
+                                                  None), 1),
+    ("h3b_rmsnorm_modulate_quant_nvfp4_noalloc", (16, 4, 1000, 1000, 16, 16, 16, 0, None, 1e-6, 16, 16, 16, 1,
+                                                  None), 1),
 ])
 def test_host_side_validation(name, args, code):
     fn = getattr(_lib.lib(), name)

@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import h3_oracle as O
@@ -32,3 +33,23 @@ def test_permute_blocked_rows_matches_dense_permutation():
     dense = O.from_blocked(qz["sf"].numpy(), rows, k // 16)
     want = O.to_blocked(dense[perm.numpy()])
     assert np.array_equal(out.numpy().reshape(-1), np.asarray(want).reshape(-1))
+
+
+def test_quantized_rows_must_match_the_layer():
+    """INT8 rows quantised ahead of a layer (QuantizedRows, e.g. from the fused
+    norm + quantise kernel) must carry the layer's ConvRot grouping; NVFP4
+    layers refuse them.  Both are host-side checks."""
+    import torch
+
+    from minixmax_h3_b200.modules import QuantizedRows, QuantLinear
+
+    w = torch.zeros(64, 256, dtype=torch.int8)
+    ql = QuantLinear.from_quant_tensors(w, meta={"format": "int8_tensorwise", "convrot": True},
+                                        weight_scale=torch.ones(64), device="cpu")
+    rows = QuantizedRows(torch.zeros(4, 256, dtype=torch.int8), torch.ones(4), convrot_group=0)
+    with pytest.raises(ValueError):
+        ql._quant_i8_input(rows)
+    ok = QuantizedRows(rows.q, rows.scale, convrot_group=256)
+    q, s = ql._quant_i8_input(ok)
+    assert q is ok.q and s is ok.scale
+    assert ok.shape == (4, 256) and ok.device.type == "cpu"
