@@ -53,3 +53,34 @@ def test_quantized_rows_must_match_the_layer():
     q, s = ql._quant_i8_input(ok)
     assert q is ok.q and s is ok.scale
     assert ok.shape == (4, 256) and ok.device.type == "cpu"
+
+
+def test_ring_attention_single_process_is_one_merge_step():
+    """Without a process group the ring runs one step: the chunk result is
+    both the first and the last merge (it initialises and finishes the fp32
+    accumulator in one call) — with the oracle's attention and merge plugged in
+    it equals attention over the local keys."""
+    import torch
+
+    from minixmax_h3_b200 import ulysses as U
+
+    calls = []
+
+    def attn(q_, k_, v_, sc, o_, lse_):
+        o, lse = O.attention_lse_fp32(q_, k_, v_, sc)
+        o_.copy_(o.to(torch.bfloat16))
+        lse_.copy_(lse)
+
+    def merge(acc, acc_lse, blk, blk_lse, first, out=None, amax_out=None):
+        calls.append((first, out is not None))
+        acc.copy_(blk.float())
+        acc_lse.copy_(blk_lse)
+        if out is not None:
+            out.copy_(acc.to(torch.bfloat16))
+
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(40, 2, 16, generator=g).to(torch.bfloat16) for _ in range(3))
+    got = U.ring_attention(q, k, v, attention_fn=attn, merge_fn=merge)
+    want, _ = O.attention_lse_fp32(q, k, v)
+    assert calls == [(True, True)]
+    assert torch.equal(got, want.to(torch.bfloat16))
