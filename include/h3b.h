@@ -12,6 +12,11 @@
  *    h3b_device_status().
  *  - Entry points allocate no device memory and never synchronise the host
  *    (h3b_device_status() excepted); callers own every buffer.
+ *  - An empty batch (zero rows / query rows) is a valid no-op returning
+ *    H3B_OK for the row-wise kernels, the plain GEMMs and attention, as the
+ *    reference's F.linear / SDPA return empty results; the sequence-parallel
+ *    variants (*_seq2head, *_head2seq) and h3b_quant_nvfp4 (whose global
+ *    scale output would be left unwritten) require rows.
  *  - bf16 = IEEE bfloat16 stored as uint16; e4m3 = OCP float8 e4m3fn; e2m1
  *    codes are 4-bit values packed two per byte.
  *

@@ -32,15 +32,9 @@ from typing import Any, Optional
 import torch
 import torch.nn as nn
 
-from .modules import Linear, QuantLinear
+from .modules import Linear, QuantLinear, decode_comfy_quant
 
 COMFY_QUANT_SUFFIX = ".comfy_quant"
-
-
-def decode_comfy_quant(blob: torch.Tensor) -> dict[str, Any]:
-    """JSON metadata stored as the bytes of a uint8 tensor
-    (modules/linear.py:243-245)."""
-    return json.loads(bytes(blob.detach().cpu().contiguous().view(torch.uint8).numpy().tobytes()).decode("utf-8"))
 
 
 def encode_comfy_quant(meta: dict[str, Any]) -> torch.Tensor:

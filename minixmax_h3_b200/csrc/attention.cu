@@ -521,7 +521,7 @@ int launch_attention(const void* q, const void* k, const void* v, AttnArgs a, in
                      int64_t s_kv, int64_t q_seq_stride, int64_t q_head_stride, int64_t kv_seq_stride,
                      int64_t kv_head_stride, float scale, cudaStream_t stream) {
   if (q == nullptr || k == nullptr || v == nullptr) return H3B_ERR_ARG;
-  if (heads <= 0 || s_q <= 0 || s_kv <= 0 || heads > 65535 || s_q > (1ll << 30) || s_kv > (1ll << 30))
+  if (heads <= 0 || s_q < 0 || s_kv <= 0 || heads > 65535 || s_q > (1ll << 30) || s_kv > (1ll << 30))
     return H3B_ERR_SHAPE;
   if (!(scale > 0.0f)) return H3B_ERR_ARG;
   const int64_t strides[6] = {q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride, a.o_seq_stride,
@@ -529,6 +529,7 @@ int launch_attention(const void* q, const void* k, const void* v, AttnArgs a, in
   for (int64_t st : strides)
     if (st <= 0 || (st % 8) != 0) return H3B_ERR_ALIGN;
   if (!h3b::aligned16(q) || !h3b::aligned16(k) || !h3b::aligned16(v)) return H3B_ERR_ALIGN;
+  if (s_q == 0) return H3B_OK;  // no query rows: nothing to write
   CUtensorMap tq, tk, tv;
   int rc = h3b::encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, D, s_q, heads, q_seq_stride * 2,
                           q_head_stride * 2, 64, BQ, 1, CU_TENSOR_MAP_SWIZZLE_128B);

@@ -676,8 +676,10 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
   return launch_gemm_t<KIND, 1>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
 }
 
+// m == 0 (an empty batch) passes: the plain GEMM entries then return
+// H3B_OK without a launch, as an empty F.linear returns an empty result.
 int check_common(int64_t m, int64_t n, int64_t k, int64_t kmul) {
-  if (m <= 0 || n <= 0 || k <= 0) return H3B_ERR_SHAPE;
+  if (m < 0 || n <= 0 || k <= 0) return H3B_ERR_SHAPE;
   if ((k % kmul) != 0 || (n % 32) != 0) return H3B_ERR_SHAPE;
   if (m > (1ll << 30) || n > (1ll << 30) || k > (1ll << 30)) return H3B_ERR_SHAPE;
   return H3B_OK;
@@ -698,6 +700,7 @@ extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* 
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
   if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(y)) return H3B_ERR_ALIGN;
   if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
   GemmArgs a{};
   a.xs = xs;
   a.ws = ws;
@@ -723,6 +726,7 @@ extern "C" int h3b_gemm_i8_acc_i32(const int8_t* q, const int8_t* w, int32_t* ac
   int rc = check_common(m, n, k, 128);
   if (rc != H3B_OK) return rc;
   if (!h3b::aligned16(q) || !h3b::aligned16(w) || !h3b::aligned16(acc)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
   GemmArgs a{};
   a.y = acc;
   a.ldy = n;
@@ -752,6 +756,7 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
       !h3b::aligned16(w_sf))
     return H3B_ERR_ALIGN;
   if (resid != nullptr && !h3b::aligned16(resid)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
   GemmArgs a{};
   a.a_gs = a_gs;
   a.w_gs = w_gs;
@@ -808,6 +813,7 @@ extern "C" int h3b_gemm_i8_seq2head(const int8_t* q, const float* xs, const int8
   if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr) return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 128);
   if (rc != H3B_OK) return rc;
+  if (m == 0) return H3B_ERR_SHAPE;  // every rank holds an equal, non-empty sequence shard
   if (!h3b::aligned16(q) || !h3b::aligned16(w)) return H3B_ERR_ALIGN;
   GemmArgs a{};
   PeerMaps maps{};
@@ -831,6 +837,7 @@ extern "C" int h3b_gemm_nvfp4_seq2head(const uint8_t* a_codes, const uint8_t* a_
     return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 256);
   if (rc != H3B_OK) return rc;
+  if (m == 0) return H3B_ERR_SHAPE;  // every rank holds an equal, non-empty sequence shard
   if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(a_sf) || !h3b::aligned16(w_sf))
     return H3B_ERR_ALIGN;
   GemmArgs a{};

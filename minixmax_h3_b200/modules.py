@@ -274,8 +274,9 @@ class QuantLinear(nn.Module):
 
 
 def decode_comfy_quant(blob: torch.Tensor) -> dict[str, Any]:
-    """Comfy ``*.comfy_quant`` JSON blob -> dict (modules/linear.py:243-245)."""
-    return json.loads(bytes(blob.detach().cpu().numpy().tobytes()).decode("utf-8"))
+    """Comfy ``*.comfy_quant`` JSON blob (the bytes of a uint8 tensor) -> dict
+    (modules/linear.py:243-245)."""
+    return json.loads(bytes(blob.detach().cpu().contiguous().view(torch.uint8).numpy().tobytes()).decode("utf-8"))
 
 
 class Ops:

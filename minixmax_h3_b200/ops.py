@@ -56,6 +56,8 @@ def quant_i8_rows(x: torch.Tensor, *, convrot_group: int = 0,
     x2, m, k, ld = _rows(x)
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    if m == 0:  # empty batch (a zero-size tensor may carry a null pointer)
+        return q, s
     dt = 0 if x.dtype == torch.bfloat16 else 1
     if convrot_group:
         if x_rot_out is not None and (x_rot_out.shape != (m, k) or x_rot_out.dtype != x.dtype
@@ -85,6 +87,8 @@ def gemm_i8(q: torch.Tensor, xs: torch.Tensor, w: torch.Tensor, ws: torch.Tensor
     if out is None:
         out = resid if epilogue == EPI_GATE_RES else torch.empty(
             (m, n // 2 if epilogue == EPI_SWIGLU else n), dtype=torch.bfloat16, device=q.device)
+    if m == 0:
+        return out
     gate_ld = _gate_ld(gate)
     call("h3b_gemm_i8_bf16", q.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), _ptr(bias), out.data_ptr(),
          out.stride(0), _ptr(resid), _ptr(gate), gate_ld, _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k,
@@ -147,6 +151,8 @@ def amax(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         raise TypeError("amax expects a contiguous bf16 tensor")
     if out is None:
         out = torch.empty((1,), dtype=torch.float32, device=x.device)
+    if x.numel() == 0:
+        return out.zero_()
     call("h3b_amax_bf16", x.data_ptr(), x.numel(), out.data_ptr(), _stream(x))
     return out
 
@@ -158,6 +164,10 @@ def quant_nvfp4(x: torch.Tensor, *, hi_first: bool = False,
     if x.dtype != torch.bfloat16:
         raise TypeError("quant_nvfp4 expects bf16 input")
     x2, m, k, ld = _rows(x)
+    if m == 0:  # an empty batch: no codes, and the global scale of an all-zero tensor
+        return NVFP4Tensor(torch.empty((0, k // 2), dtype=torch.uint8, device=x.device),
+                           torch.empty((0,), dtype=torch.uint8, device=x.device),
+                           torch.ones((1,), dtype=torch.float32, device=x.device), 0, k, hi_first)
     if amax_t is None:
         amax_t = amax(x2 if x2.is_contiguous() else x2.contiguous())
     codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
@@ -237,6 +247,8 @@ def gemm_nvfp4(a: NVFP4Tensor, w: NVFP4Tensor, bias: Optional[torch.Tensor] = No
     if out is None:
         out = resid if epilogue == EPI_GATE_RES else torch.empty(
             (m, n // 2 if epilogue == EPI_SWIGLU else n), dtype=torch.bfloat16, device=a.codes.device)
+    if m == 0:
+        return out
     call("h3b_gemm_nvfp4_bf16", a.codes.data_ptr(), a.sf.data_ptr(), a.gs.data_ptr(), w.codes.data_ptr(),
          w.sf.data_ptr(), w.gs.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0), _ptr(resid), _ptr(gate),
          _gate_ld(gate), _ptr(row_sel), _ptr(amax_out), epilogue, m, n, k, _stream(a.codes))
@@ -264,6 +276,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optio
     s_kv = k.shape[0]
     if out is None:
         out = torch.empty((s_q, heads, d), dtype=torch.bfloat16, device=q.device)
+    if s_q == 0:
+        return out
     scale = d ** -0.5 if scale is None else float(scale)
     call("h3b_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse), _ptr(amax_out),
          heads, s_q,

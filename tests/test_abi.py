@@ -59,3 +59,17 @@ def test_library_exports_every_symbol():
 def test_host_side_validation(name, args, code):
     fn = getattr(_lib.lib(), name)
     assert fn(*args) == code
+
+
+@pytest.mark.parametrize("name,args", [
+    ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 0, 0, 64, 128, None)),
+    ("h3b_gemm_i8_acc_i32", (16, 16, 16, 0, 64, 128, None)),
+    ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 192, None, None, 0, None, None, 0, 0, 192, 256, None)),
+    ("h3b_attention_fwd", (16,) * 4 + (None, None, 2, 0, 128, 128, 128, 128, 128, 128, 128, 0.1, None)),
+    ("h3b_quant_i8_rows", (16, 0, 0, 64, 64, 16, 16, None)),
+])
+def test_empty_batch_is_a_no_op(name, args):
+    """Zero rows: H3B_OK before any launch (the reference returns an empty
+    result for an empty batch)."""
+    fn = getattr(_lib.lib(), name)
+    assert fn(*args) == 0

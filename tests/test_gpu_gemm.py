@@ -155,3 +155,23 @@ def test_swiglu_epilogue(cuda, fmt, m, ffn, k):
     assert amax.item() == got.float().abs().max().item()
     # the plain forward still returns the reference's [gate | up] column order
     assert torch.equal(ql(x), full)
+
+
+@pytest.mark.parametrize("fmt", ["int8_tensorwise", "nvfp4"])
+def test_quant_linear_empty_batch(cuda, fmt):
+    """An empty batch gives an empty result, as F.linear does in the
+    reference's fallback (int8_convrot.py:199-209): no kernel fails on zero
+    rows."""
+    from minixmax_h3_b200 import ops
+    from minixmax_h3_b200.block import load_quant_linear
+    from minixmax_h3_b200.modules import QuantLinear
+
+    ql = QuantLinear(512, 384, bias=False, device=cuda)
+    load_quant_linear(ql, torch.randn(384, 512, device=cuda) * 0.02, fmt)
+    x = torch.empty(0, 512, dtype=torch.bfloat16, device=cuda)
+    assert ql(x).shape == (0, 384)
+    assert ql.forward_fused(x).shape == (0, 384)
+    q = torch.randn(0, 2, 128, device=cuda).to(torch.bfloat16)
+    kv = torch.randn(64, 2, 128, device=cuda).to(torch.bfloat16)
+    assert ops.attention(q, kv, kv).shape == (0, 2, 128)
+    torch.cuda.synchronize()
