@@ -119,6 +119,53 @@ def test_nvfp4_gemm(cuda, m, n, k):
     assert_close_bf16(y, F.linear(ad, wd, bias).float(), max_abs=5e-2)
 
 
+def test_nvfp4_cfg3_shapes_sampled(cuda):
+    """BASELINE cfg 3 shapes at full M=32768: the whole activation and weight
+    quantised on the GPU, then two 128-row groups of each (group 0 holds the
+    planted global max, so a CPU quantiser of just those rows sees the same
+    global scale) checked bit-exact in codes and blocked scales, and the
+    GEMM's outputs at those rows and columns held to the float bar against
+    the exact product of the decoded operands."""
+    from minixmax_h3_b200 import ops
+
+    m = 32768
+    gen = torch.Generator().manual_seed(3)
+
+    def sample(count):
+        groups = [0, int(torch.randint(1, count // 128, (1,), generator=gen))]
+        return groups, torch.cat([torch.arange(g * 128, g * 128 + 128) for g in groups])
+
+    def check_rows(t, src, groups, rows, k):
+        ref = O.nvfp4_quantize(src[rows.to(cuda)].cpu(), hi_first=False)
+        chunk = (k // 16 + 3) // 4 * 512  # blocked scale bytes of one 128-row group
+        assert torch.equal(t.gs.cpu(), ref["gs"])
+        assert torch.equal(t.codes[rows.to(cuda)].cpu(), ref["codes"])
+        assert torch.equal(torch.cat([t.sf[g * chunk:(g + 1) * chunk] for g in groups]).cpu(), ref["sf"])
+        return ref
+
+    xg, xrows = sample(m)
+    for k, n in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]:
+        g = torch.Generator(device=cuda).manual_seed(k + n)
+        x = torch.randn(m, k, generator=g, device=cuda)
+        x = torch.where(torch.rand(m, k, generator=g, device=cuda) < 0.001, 20 * x, x)
+        x[0, 5] = 1000.0
+        x = x.to(torch.bfloat16)
+        w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+        w[0, 7] = 1.0
+        w = w.to(torch.bfloat16)
+        bias = (torch.randn(n, generator=g, device=cuda) * 0.1).to(torch.bfloat16)
+        a = ops.quant_nvfp4(x, hi_first=False)
+        wq = ops.quant_nvfp4(w, hi_first=False)
+        y = ops.gemm_nvfp4(a, wq, bias)
+
+        wg, wrows = sample(n)
+        a_ref = check_rows(a, x, xg, xrows, k)
+        w_ref = check_rows(wq, w, wg, wrows, k)
+        exact = O.nvfp4_linear_w4a4(a_ref, w_ref, k, bias[wrows.to(cuda)].cpu(), a_hi_first=False,
+                                    w_hi_first=False)
+        assert_close_bf16(y[xrows.to(cuda)][:, wrows.to(cuda)], exact)
+
+
 def _bf16_ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return (a.view(torch.int16).int() - b.view(torch.int16).int()).abs()
 

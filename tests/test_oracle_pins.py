@@ -93,6 +93,25 @@ def test_nvfp4_golden():
     assert torch.equal(O.swap_nibbles(lo["codes"]), g["codes_hi_first"])
 
 
+def test_nvfp4_row_group_sampling():
+    """The full-size GPU checks quantise only sampled 128-row groups on the
+    CPU.  That equals slicing the whole tensor's quantisation when the group
+    holding the global max is among them, and each group's blocked scales
+    are one contiguous chunk of (k/16 rounded up to 4) * 128 bytes."""
+    gen = torch.Generator().manual_seed(5)
+    m, k = 640, 208  # k/16 = 13 scale columns: the last 4-column block is padded
+    x = torch.randn(m, k, generator=gen)
+    x[130, 17] = 50.0
+    full = O.nvfp4_quantize(x.to(torch.bfloat16), hi_first=False)
+    groups = [1, 3]
+    rows = torch.cat([torch.arange(g * 128, g * 128 + 128) for g in groups])
+    part = O.nvfp4_quantize(x[rows].to(torch.bfloat16), hi_first=False)
+    chunk = (k // 16 + 3) // 4 * 512
+    assert torch.equal(part["gs"], full["gs"])
+    assert torch.equal(part["codes"], full["codes"][rows])
+    assert torch.equal(part["sf"], torch.cat([full["sf"][g * chunk:(g + 1) * chunk] for g in groups]))
+
+
 # ---------------------------------------------------------------- RoPE / norm
 
 def test_rope_golden():
