@@ -3,7 +3,14 @@ committed golden fixtures (generated from the reference by
 tests/golden/make_golden.py)."""
 from __future__ import annotations
 
+import importlib.util
+import json
+import subprocess
+import sys
+from pathlib import Path
+
 import numpy as np
+import pytest
 import torch
 
 from helpers import load_golden
@@ -91,6 +98,27 @@ def test_nvfp4_golden():
     assert torch.equal(O.nvfp4_dequantize(qz["codes"], qz["gs"], qz["sf"], k), g["dequant_f32"])
     lo = O.nvfp4_quantize(g["x"], hi_first=False)
     assert torch.equal(O.swap_nibbles(lo["codes"]), g["codes_hi_first"])
+
+
+@pytest.mark.skipif(importlib.util.find_spec("vllm") is None, reason="vllm not installed")
+def test_nvfp4_quantiser_vs_independent_implementation():
+    """The reference's own NVFP4 quantiser is not in its sources, so the
+    oracle's is compared with an independent one, vllm's pure-torch
+    ref_nvfp4_quant (run in a child process by nvfp4_vllm_xcheck.py).  The
+    two must agree on every block scale and code except at exact rounding
+    ties, where the recipes' different fp32 orders (divide vs multiply by a
+    reciprocal) decide; there they may differ by one step.  The weights case
+    is built to contain such ties, so that path is exercised."""
+    script = Path(__file__).with_name("nvfp4_vllm_xcheck.py")
+    out = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-3000:]
+    result = json.loads(out.stdout.strip().splitlines()[-1])
+    for name, c in result.items():
+        assert c["scale_tie_dist_max"] == 0.0 and c["code_tie_dist_max"] == 0.0, (name, c)
+        assert c["scale_steps_apart_max"] <= 1, (name, c)
+        assert c["scale_mismatches"] <= 0.02 * c["scales"], (name, c)
+        assert c["code_mismatches"] <= 0.002 * c["codes_compared"], (name, c)
+    assert result["weights"]["scale_mismatches"] > 0
 
 
 def test_nvfp4_row_group_sampling():
