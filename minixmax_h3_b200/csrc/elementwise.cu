@@ -100,11 +100,11 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
   }
 }
 
-// CTAs of 256 threads stride over rows; a row is held in registers (<= MAXV
-// x 8 bf16 per thread).  The optional |h| max is reduced per CTA and published
-// with one atomic.
-template <int MAXV>
-__global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
+// CTAs of THREADS threads stride over rows; a row is held in registers
+// (<= MAXV x 8 bf16 per thread).  The optional |h| max is reduced per CTA and
+// published with one atomic.
+template <int THREADS, int MAXV>
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 8 : 1) rmsnorm_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ h, int64_t m, int64_t hidden, int64_t ld,
     const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ shift,
     const __nv_bfloat16* __restrict__ scale, int64_t tab_ld, const int32_t* __restrict__ row_sel, float eps,
@@ -119,12 +119,12 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
     const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     uint4 v[MAXV];
-    amax = fmaxf(amax, h3b::rmsnorm_modulate_row<MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r,
+    amax = fmaxf(amax, h3b::rmsnorm_modulate_row<THREADS, MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r,
                                                        modulate, red, v));
     __nv_bfloat16* hr = h + row * ld;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * 256;
+      const int vi = threadIdx.x + i * THREADS;
       if (vi < nvec) *reinterpret_cast<uint4*>(hr + vi * 8) = v[i];
     }
   }
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(
     if (lane == 0) red[warp] = amax;
     __syncthreads();
     if (warp == 0) {
-      float t = lane < 8 ? red[lane] : 0.0f;
+      float t = lane < THREADS / 32 ? red[lane] : 0.0f;
       t = warp_max(t);
       if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), __float_as_uint(t));
     }
@@ -265,15 +265,17 @@ extern "C" int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t h
   const auto* sh = static_cast<const __nv_bfloat16*>(shift);
   const auto* sc = static_cast<const __nv_bfloat16*>(scale);
   const int64_t nvec = hidden / 8;
-  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * 8;
+  // rows up to 3072 wide: 128-thread CTAs (8 per SM, one row each in flight)
+  const bool narrow = nvec <= 128 * 3;
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * (narrow ? 16 : 8);
   if (blocks > m) blocks = m;
   const unsigned g = static_cast<unsigned>(blocks);
-  if (nvec <= 256 * 2)
-    rmsnorm_modulate_kernel<2><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
-                                                  amax_out);
+  if (narrow)
+    rmsnorm_modulate_kernel<128, 3><<<g, 128, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
+                                                       amax_out);
   else if (nvec <= 256 * 8)
-    rmsnorm_modulate_kernel<8><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
-                                                  amax_out);
+    rmsnorm_modulate_kernel<256, 8><<<g, 256, 0, st>>>(xb, hb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel, eps,
+                                                       amax_out);
   else
     return H3B_ERR_SHAPE;
   return h3b::launch_status();

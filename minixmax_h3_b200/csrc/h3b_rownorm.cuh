@@ -6,9 +6,10 @@
 //   h = n                                           for rows outside every segment.
 // Shared by the stand-alone kernel and the fused quantising kernels so that
 // both produce the same bits (same element-to-thread map, same reduction
-// order).  A 256-thread CTA holds the row in registers: thread t keeps
-// elements 8(t + 256 i) .. +7 of the row in v[i] (i < MAXV), so warp w's
-// chunk i is the 256 consecutive elements starting at 256 (w + 8 i).
+// order).  A CTA of THREADS threads holds the row in registers: thread t
+// keeps elements 8(t + THREADS i) .. +7 of the row in v[i] (i < MAXV), so
+// warp w's chunk i is the 256 consecutive elements starting at
+// 256 (w + (THREADS / 32) i).
 #pragma once
 
 #include "h3b_common.cuh"
@@ -18,7 +19,7 @@ namespace h3b {
 // Loads row xr into v (bf16 x) and leaves the modulated bf16 h there;
 // returns max |h| over this thread's elements.  red: 33 floats of shared
 // memory; the call holds three CTA barriers.
-template <int MAXV>
+template <int THREADS, int MAXV>
 H3B_DEV float rmsnorm_modulate_row(const __nv_bfloat16* __restrict__ xr, int nvec, int64_t hidden, float eps,
                                    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ shift_r,
                                    const __nv_bfloat16* __restrict__ scale_r, bool modulate, float* red,
@@ -27,7 +28,7 @@ H3B_DEV float rmsnorm_modulate_row(const __nv_bfloat16* __restrict__ xr, int nve
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
-    const int vi = threadIdx.x + i * 256;
+    const int vi = threadIdx.x + i * THREADS;
     if (vi < nvec) {
       v[i] = *reinterpret_cast<const uint4*>(xr + vi * 8);
       const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
@@ -42,7 +43,7 @@ H3B_DEV float rmsnorm_modulate_row(const __nv_bfloat16* __restrict__ xr, int nve
   if (lane == 0) red[warp] = ss;
   __syncthreads();
   if (warp == 0) {
-    float t = lane < 8 ? red[lane] : 0.0f;
+    float t = lane < THREADS / 32 ? red[lane] : 0.0f;
     t = warp_sum(t);
     if (lane == 0) red[32] = t;
   }
@@ -52,7 +53,7 @@ H3B_DEV float rmsnorm_modulate_row(const __nv_bfloat16* __restrict__ xr, int nve
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
-    const int vi = threadIdx.x + i * 256;
+    const int vi = threadIdx.x + i * THREADS;
     if (vi < nvec) {
       const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
       const uint4 sh = *reinterpret_cast<const uint4*>(shift_r + vi * 8);

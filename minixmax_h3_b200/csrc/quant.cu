@@ -428,10 +428,10 @@ int launch_quant_i8(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q,
 // bf16 output (int8_convrot.py:114-157 on the output of dit.py:433-434),
 // without writing that output: the row stays in registers.  In the row
 // layout of rmsnorm_modulate_row, warp w's chunk i is exactly ConvRot group
-// w + 8 i with element 8 lane + e in lane `lane`, the order
+// w + (THREADS / 32) i with element 8 lane + e in lane `lane`, the order
 // hadamard256_warp rotates, so ROT needs no data movement.
-template <int MAXV, bool ROT>
-__global__ void __launch_bounds__(256) rmsnorm_modulate_quant_i8_kernel(
+template <int THREADS, int MAXV, bool ROT>
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? (ROT ? 6 : 8) : 1) rmsnorm_modulate_quant_i8_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t m, int64_t hidden, int64_t ld, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale, int64_t tab_ld,
     const int32_t* __restrict__ row_sel, float eps, int8_t* __restrict__ q, float* __restrict__ q_scale) {
@@ -443,12 +443,12 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_quant_i8_kernel(
     const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     uint4 v[MAXV];
-    float amax = h3b::rmsnorm_modulate_row<MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r, modulate,
+    float amax = h3b::rmsnorm_modulate_row<THREADS, MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r, modulate,
                                                  red, v);
     float f[MAXV][8];
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * 256;
+      const int vi = threadIdx.x + i * THREADS;
       if (vi < nvec) {  // warp-uniform when ROT (hidden % 256 == 0)
         unpack8<__nv_bfloat16>(v[i], f[i]);
         if constexpr (ROT) {
@@ -465,13 +465,13 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_quant_i8_kernel(
       amax = 0.0f;
 #pragma unroll
       for (int i = 0; i < MAXV; ++i) {
-        if (threadIdx.x + i * 256 < nvec) {
+        if (threadIdx.x + i * THREADS < nvec) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[i][e]));
         }
       }
     }
-    amax = block_max<256>(amax, red);
+    amax = block_max<THREADS>(amax, red);
     amax = fmaxf(amax, 1e-12f);
     const float s = __fdiv_rn(amax, 127.0f);
     const bool fast = rcp_div_ok(s);
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_quant_i8_kernel(
     int8_t* qr = q + row * hidden;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * 256;
+      const int vi = threadIdx.x + i * THREADS;
       if (vi < nvec) {
         uint32_t packed[2] = {0u, 0u};
 #pragma unroll
@@ -594,24 +594,26 @@ extern "C" int h3b_rmsnorm_modulate_quant_i8(const void* x, int64_t m, int64_t h
   const auto* sh = static_cast<const __nv_bfloat16*>(shift);
   const auto* sc = static_cast<const __nv_bfloat16*>(scale);
   const int64_t nvec = hidden / 8;
-  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * 8;
+  // rows up to 3072 wide: 128-thread CTAs (8 per SM, one row each in flight)
+  const bool narrow = nvec <= 128 * 3;
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * (narrow ? 16 : 8);
   if (blocks > m) blocks = m;
   const unsigned g = static_cast<unsigned>(blocks);
   const bool rot = convrot_group == 256;
-  if (nvec <= 256 * 2) {
+  if (narrow) {
     if (rot)
-      rmsnorm_modulate_quant_i8_kernel<2, true><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
-                                                                   eps, q, q_scale);
+      rmsnorm_modulate_quant_i8_kernel<128, 3, true><<<g, 128, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld,
+                                                                        row_sel, eps, q, q_scale);
     else
-      rmsnorm_modulate_quant_i8_kernel<2, false><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
-                                                                    eps, q, q_scale);
+      rmsnorm_modulate_quant_i8_kernel<128, 3, false><<<g, 128, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld,
+                                                                         row_sel, eps, q, q_scale);
   } else if (nvec <= 256 * 8) {
     if (rot)
-      rmsnorm_modulate_quant_i8_kernel<8, true><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
-                                                                   eps, q, q_scale);
+      rmsnorm_modulate_quant_i8_kernel<256, 8, true><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld,
+                                                                        row_sel, eps, q, q_scale);
     else
-      rmsnorm_modulate_quant_i8_kernel<8, false><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld, row_sel,
-                                                                    eps, q, q_scale);
+      rmsnorm_modulate_quant_i8_kernel<256, 8, false><<<g, 256, 0, st>>>(xb, m, hidden, ld, wb, sh, sc, tab_ld,
+                                                                         row_sel, eps, q, q_scale);
   } else {
     return H3B_ERR_SHAPE;
   }

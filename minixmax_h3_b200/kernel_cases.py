@@ -8,6 +8,8 @@
     python -m minixmax_h3_b200.kernel_cases quant_i8_convrot --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases qk_rope --seq 131072 --heads 24
     python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate --m 131072 --k 3072
+    python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate_quant_i8 --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate_quant_i8_convrot --m 32768 --k 3072
 
 Each case allocates its inputs once, launches the kernel `--warmup` times,
 then `--iters` times between CUDA events on the launching stream, and prints
@@ -41,7 +43,8 @@ def _time(fn, warmup: int, iters: int) -> float:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8",
-                                       "quant_i8_convrot", "qk_rope", "rmsnorm_modulate"])
+                                       "quant_i8_convrot", "qk_rope", "rmsnorm_modulate", "rmsnorm_modulate_quant_i8",
+                                       "rmsnorm_modulate_quant_i8_convrot"])
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--heads", type=int, default=24)
     ap.add_argument("--m", type=int, default=8192)
@@ -87,6 +90,19 @@ def main() -> None:
                                                rope.n_t, rope.n_h), a.warmup, a.iters)
         nbytes = 2 * 2 * a.seq * a.heads * 128 * 2 + a.seq * 3 * 4  # q, k read + written; positions
         rec.update(seq=a.seq, heads=a.heads, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
+    elif a.case.startswith("rmsnorm_modulate_quant_i8"):
+        x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.ones(a.k, dtype=torch.bfloat16, device=dev)
+        tab = (torch.randn(2, 2 * a.k, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        row_sel = torch.zeros(a.m, dtype=torch.int32, device=dev)
+        q = torch.empty(a.m, a.k, dtype=torch.int8, device=dev)
+        xs = torch.empty(a.m, dtype=torch.float32, device=dev)
+        group = 256 if a.case.endswith("convrot") else 0
+        ms = _time(lambda: ops.rmsnorm_modulate_quant_i8(x, w, tab[:, : a.k], tab[:, a.k:], 1e-6, row_sel=row_sel,
+                                                         convrot_group=group, q_out=q, scale_out=xs),
+                   a.warmup, a.iters)
+        nbytes = 2 * a.m * a.k + a.m * a.k + 4 * a.m + 4 * a.m  # x read, codes, row scales, row indices
+        rec.update(m=a.m, k=a.k, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
     elif a.case == "rmsnorm_modulate":
         x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
         w = torch.ones(a.k, dtype=torch.bfloat16, device=dev)
