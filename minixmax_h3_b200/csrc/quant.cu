@@ -75,6 +75,15 @@ H3B_DEV float div_rn_by_rcp(float a, float b, float y) {
 
 H3B_DEV bool rcp_div_ok(float b) { return b >= 0x1p-96f && b <= 0x1p96f; }
 
+// A divisor in [2^-86, 2^96] lets every element of its row or block take the
+// Markstein quotient, with no per-element guard.  An element with
+// |a| < 2^-90, whose residual may underflow, has |a / b| < 2^-4, and the
+// corrected value stays below 2^-4 + 2^-3: both give a zero code (rint of
+// less than 1/2 for INT8, e2m1 of less than 1/4).  The sign of that zero:
+// a -0 dividend comes out +0, so e2m1 callers restore it with copysign (a
+// no-op for every non-zero dividend, whose quotient keeps its sign).
+H3B_DEV bool rcp_div_ok_all(float b) { return b >= 0x1p-86f && b <= 0x1p96f; }
+
 template <typename T, int THREADS, int MAXV>
 __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restrict__ x, int64_t k, int64_t ldx,
                                                                 int8_t* __restrict__ q, float* __restrict__ scale) {
@@ -98,7 +107,7 @@ __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restr
   amax = block_max<THREADS>(amax, red);
   amax = fmaxf(amax, 1e-12f);
   const float s = __fdiv_rn(amax, 127.0f);
-  const bool fast = rcp_div_ok(s);
+  const bool fast = rcp_div_ok_all(s);  // s >= 1e-12 / 127 > 2^-47
   const float y = __frcp_rn(s);
   int8_t* qr = q + row * k;
 #pragma unroll
@@ -110,7 +119,7 @@ __global__ void __launch_bounds__(THREADS) quant_i8_rows_kernel(const T* __restr
       uint32_t packed[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float r = rintf((fast && fabsf(f[j]) >= 0x1p-90f) ? div_rn_by_rcp(f[j], s, y) : __fdiv_rn(f[j], s));
+        float r = rintf(fast ? div_rn_by_rcp(f[j], s, y) : __fdiv_rn(f[j], s));
         r = fminf(fmaxf(r, -128.0f), 127.0f);
         const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
         packed[j >> 2] |= b << ((j & 3) * 8);
@@ -237,7 +246,7 @@ __global__ void __launch_bounds__(256) quant_i8_rows_rot_kernel(const T* __restr
   amax = block_max<256>(amax, red);
   amax = fmaxf(amax, 1e-12f);
   const float s = __fdiv_rn(amax, 127.0f);
-  const bool fast = rcp_div_ok(s);
+  const bool fast = rcp_div_ok_all(s);  // s >= 1e-12 / 127 > 2^-47
   const float y = __frcp_rn(s);
   int8_t* qr = q + row * k;
 #pragma unroll
@@ -248,7 +257,7 @@ __global__ void __launch_bounds__(256) quant_i8_rows_rot_kernel(const T* __restr
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float fj = f[i][j];
-        float r = rintf((fast && fabsf(fj) >= 0x1p-90f) ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
+        float r = rintf(fast ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
         r = fminf(fmaxf(r, -128.0f), 127.0f);
         const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
         packed[j >> 2] |= b << ((j & 3) * 8);
@@ -377,11 +386,16 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
     const float denom = sval * gs;
     float r[16];
     if (sval > 0.0f) {
-      const bool ok = rcp_div_ok(denom);
       const float y = __frcp_rn(denom);
+      if (rcp_div_ok_all(denom)) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        r[j] = (ok && fabsf(f[j]) >= 0x1p-90f) ? div_rn_by_rcp(f[j], denom, y) : __fdiv_rn(f[j], denom);
+        for (int j = 0; j < 16; ++j) r[j] = copysignf(div_rn_by_rcp(f[j], denom, y), f[j]);
+      } else {  // blocks of tiny magnitude (or a huge divisor): per-element guard
+        const bool ok = rcp_div_ok(denom);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          r[j] = (ok && fabsf(f[j]) >= 0x1p-90f) ? div_rn_by_rcp(f[j], denom, y) : __fdiv_rn(f[j], denom);
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) r[j] = 0.0f;  // an all-zero block: every code is +0
@@ -474,7 +488,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? (ROT ? 6 : 8) : 1) r
     amax = block_max<THREADS>(amax, red);
     amax = fmaxf(amax, 1e-12f);
     const float s = __fdiv_rn(amax, 127.0f);
-    const bool fast = rcp_div_ok(s);
+    const bool fast = rcp_div_ok_all(s);  // s >= 1e-12 / 127 > 2^-47
     const float y = __frcp_rn(s);
     int8_t* qr = q + row * hidden;
 #pragma unroll
@@ -485,7 +499,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? (ROT ? 6 : 8) : 1) r
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float fj = f[i][j];
-          float r = rintf((fast && fabsf(fj) >= 0x1p-90f) ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
+          float r = rintf(fast ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
           r = fminf(fmaxf(r, -128.0f), 127.0f);
           const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
           packed[j >> 2] |= b << ((j & 3) * 8);
