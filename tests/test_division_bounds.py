@@ -26,7 +26,8 @@ def _fma32(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
 
 
 def _markstein(a: np.ndarray, b: np.ndarray) -> np.ndarray:
-    with np.errstate(over="ignore", under="ignore"):
+    # quotients that overflow fp32 end as inf / nan here; callers drop them
+    with np.errstate(over="ignore", under="ignore", invalid="ignore"):
         y = (F32(1) / b).astype(np.float32)
         q0 = (a * y).astype(np.float32)
         r = _fma32(-q0, b, a)
