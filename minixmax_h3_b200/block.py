@@ -319,8 +319,9 @@ class DiTBlock(nn.Module):
         for i, (norm, shift, scale, gate, sub, ql) in enumerate((
                 (self.norm1, shift_msa, scale_msa, gate_msa, self.attn, self.attn.qkv_proj),
                 (self.norm2, shift_mlp, scale_mlp, gate_mlp, self.mlp, self.mlp.fc1))):
-            if ql.quant_format == "int8_tensorwise":
+            if ql.quant_format == "int8_tensorwise" and ql.pre_quant_scale is None:
                 # norm + modulate + (ConvRot) + row quantisation in one kernel
+                # (a pre_quant_scale applies between the two: the layer does it)
                 group = ql.group_size if ql.convrot else 0
                 q, xs = ops.rmsnorm_modulate_quant_i8(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
                                                       convrot_group=group,

@@ -216,14 +216,34 @@ class QuantLinear(nn.Module):
     def _bias(self, x) -> Optional[torch.Tensor]:
         return None if self.bias is None or self.bias.numel() == 0 else self.bias.to(torch.bfloat16)
 
+    def _pre_scale(self, x, amax: Optional[torch.Tensor]):
+        """The reference multiplies a layer's input by ``pre_quant_scale``
+        before quantising it (modules/linear.py:184-185).  Returns the scaled
+        input and the amax still valid for it: a max of the unscaled input
+        (from the producing kernel) no longer is, so it is dropped."""
+        if self.pre_quant_scale is None:
+            return x, amax
+        if isinstance(x, QuantizedRows):
+            raise ValueError("this layer has a pre_quant_scale: it needs the bf16 input, not rows already quantised")
+        return x * self.pre_quant_scale.to(device=x.device, dtype=x.dtype), None
+
     def forward_fused(self, x: torch.Tensor, *, amax: Optional[torch.Tensor] = None, epilogue: int = EPI_STORE,
                       resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
                       row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Quantise x [m, K] bf16 and run the GEMM with a fused epilogue.
+        """Quantise x [m, K] bf16 (after ``pre_quant_scale``, when the layer has
+        one) and run the GEMM with a fused epilogue.
 
         amax: precomputed max|x| (fp32 device scalar) for the NVFP4 global
         scale, e.g. from the producing kernel; computed here when None."""
+        x, amax = self._pre_scale(x, amax)
+        return self._run(x, amax=amax, epilogue=epilogue, resid=resid, gate=gate, row_sel=row_sel,
+                         amax_out=amax_out, out=out)
+
+    def _run(self, x, *, amax: Optional[torch.Tensor] = None, epilogue: int = EPI_STORE,
+             resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+             row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.quant_format == "int8_tensorwise":
             q, xs = self._quant_i8_input(x)
             return ops.gemm_i8(q, xs, self.weight_i8, self.weight_scale, self._bias(x), epilogue=epilogue,
@@ -242,6 +262,7 @@ class QuantLinear(nn.Module):
         """QKV projection of this rank's tokens stored straight into every head
         owner's receive buffer (ops.gemm_*_seq2head): the projection and the
         seq->head Ulysses exchange in one kernel."""
+        x, amax = self._pre_scale(x, amax)
         if self.quant_format == "int8_tensorwise":
             q, xs = self._quant_i8_input(x)
             ops.gemm_i8_seq2head(q, xs, self.weight_i8, self.weight_scale, self._bias(x), recv_ptrs, rank, heads)
@@ -267,7 +288,7 @@ class QuantLinear(nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         if self.quant_format == "nvfp4" or x2.dtype != torch.float16:
             x2 = x2.to(torch.bfloat16)
-        y = self.forward_fused(x2)
+        y = self._run(x2)  # pre_quant_scale applied above, before the dtype cast, as the reference does
         if self._row_perm is not None:  # interleaved for the fused SwiGLU: reference column order
             y = y[:, self._inv_perm]
         return y.to(out_dtype).reshape(*lead, self.out_features)

@@ -222,3 +222,27 @@ def test_quant_linear_empty_batch(cuda, fmt):
     kv = torch.randn(64, 2, 128, device=cuda).to(torch.bfloat16)
     assert ops.attention(q, kv, kv).shape == (0, 2, 128)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("fmt", ["int8_tensorwise", "nvfp4"])
+def test_pre_quant_scale_on_the_fused_entry(cuda, fmt):
+    """A layer with a checkpoint pre_quant_scale (modules/linear.py:184-185)
+    gives, through forward_fused (the entry the block uses) and given the
+    unscaled input's amax, the same bits as a layer without the scale fed
+    x * pre_quant_scale; forward() agrees."""
+    from minixmax_h3_b200 import ops
+    from minixmax_h3_b200.block import load_quant_linear
+    from minixmax_h3_b200.modules import QuantLinear
+
+    g = torch.Generator(device=cuda).manual_seed(4)
+    w = torch.randn(384, 512, generator=g, device=cuda) * 0.02
+    plain = QuantLinear(512, 384, bias=False, device=cuda)
+    load_quant_linear(plain, w, fmt)
+    scaled = QuantLinear(512, 384, bias=False, device=cuda)
+    load_quant_linear(scaled, w, fmt)
+    scaled.pre_quant_scale = torch.linspace(0.25, 4.0, 512, device=cuda)
+    x = torch.randn(200, 512, generator=g, device=cuda).to(torch.bfloat16)
+    xs = x * scaled.pre_quant_scale.to(torch.bfloat16)
+    stale_amax = ops.amax(x)
+    assert torch.equal(scaled.forward_fused(x, amax=stale_amax), plain.forward_fused(xs))
+    assert torch.equal(scaled(x), plain(xs))

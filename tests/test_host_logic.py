@@ -55,6 +55,34 @@ def test_quantized_rows_must_match_the_layer():
     assert ok.shape == (4, 256) and ok.device.type == "cpu"
 
 
+def test_pre_quant_scale_applies_on_every_entry():
+    """A checkpoint's pre_quant_scale multiplies the layer input before it is
+    quantised (modules/linear.py:184-185) on the block's entries too: the
+    input is scaled, a producer's amax of the unscaled input is dropped, and
+    rows that arrive already quantised are refused.  Without the scale the
+    input and amax pass through untouched."""
+    import torch
+
+    from minixmax_h3_b200.modules import QuantizedRows, QuantLinear
+
+    w = torch.zeros(64, 256, dtype=torch.int8)
+    ql = QuantLinear.from_quant_tensors(w, meta={"format": "int8_tensorwise"}, weight_scale=torch.ones(64),
+                                        device="cpu")
+    x = torch.randn(4, 256).to(torch.bfloat16)
+    amax = torch.ones(1)
+    same, same_amax = ql._pre_scale(x, amax)
+    assert same is x and same_amax is amax
+
+    pqs = torch.linspace(0.5, 2.0, 256)
+    ql = QuantLinear.from_quant_tensors(w, meta={"format": "int8_tensorwise"}, weight_scale=torch.ones(64),
+                                        pre_quant_scale=pqs, device="cpu")
+    scaled, dropped = ql._pre_scale(x, amax)
+    assert dropped is None
+    assert torch.equal(scaled, x * pqs.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        ql._pre_scale(QuantizedRows(torch.zeros(4, 256, dtype=torch.int8), torch.ones(4)), None)
+
+
 def test_ring_attention_single_process_is_one_merge_step():
     """Without a process group the ring runs one step: the chunk result is
     both the first and the last merge (it initialises and finishes the fp32
