@@ -18,6 +18,9 @@ schemes (``H3B_ULYSSES``):
   no head exchange; K and V of all tokens are gathered once
   (``all_gather_kv``, runtime/dist.py:291-312) and every rank attends its
   own queries over all keys, all heads.
+
+``H3B_CHECK_SHAPES=1`` makes every exchange first confirm that all ranks send
+messages of one shape (``_shapes_agree``).
 """
 from __future__ import annotations
 
@@ -108,6 +111,31 @@ def phase_barrier(device: torch.device, flag: Optional[torch.Tensor] = None) -> 
     tdist.all_reduce(flag, op=tdist.ReduceOp.MAX, group=state().group)
 
 
+def _shapes_agree(t: torch.Tensor) -> None:
+    """With ``H3B_CHECK_SHAPES=1``: before an exchange, every rank's message
+    (shape and element size) must match, else every rank raises the same
+    RuntimeError.  Without the check a mismatch is not a clean error: gloo
+    aborts the receiving process (its pair size check ends in
+    std::terminate) and NCCL moves the wrong bytes.  Costs one small
+    all_gather per exchange, so it is off by default."""
+    if os.environ.get("H3B_CHECK_SHAPES", "0") != "1":
+        return
+    st = state()
+    dims = list(t.shape)
+    if len(dims) > 6:
+        raise RuntimeError(f"_shapes_agree: {len(dims)}-d message, at most 6 dims are described")
+    mine = torch.tensor([t.dim(), t.element_size()] + dims + [-1] * (6 - len(dims)), dtype=torch.int64,
+                        device=t.device)
+    everyone = torch.empty(st.world_size * 8, dtype=torch.int64, device=t.device)
+    tdist.all_gather_into_tensor(everyone, mine, group=st.group)
+    rows = everyone.view(st.world_size, 8).cpu().tolist()
+    for r, row in enumerate(rows):
+        if row != rows[0]:
+            def desc(v):
+                return f"shape {tuple(v[2:2 + v[0]])} of {v[1]}-byte elements"
+            raise RuntimeError(f"exchange mismatch: rank 0 sends {desc(rows[0])}, rank {r} sends {desc(row)}")
+
+
 def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
     """gather_seq=True: [S_local, H, D] -> [S, H/ws, D];
     gather_seq=False: [S, H/ws, D] -> [S_local, H, D]  (ops/ulysses.py:14-41)."""
@@ -121,6 +149,7 @@ def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
             raise RuntimeError(f"heads={heads} not divisible by world_size={ws}")
         h_local = heads // ws
         send = x.view(s_local, ws, h_local, dim).permute(1, 0, 2, 3).contiguous()
+        _shapes_agree(send)
         recv = torch.empty_like(send)
         tdist.all_to_all_single(recv, send, group=group)
         return recv.reshape(ws * s_local, h_local, dim)
@@ -129,6 +158,7 @@ def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
         raise RuntimeError(f"seq={seq} not divisible by world_size={ws}")
     s_local = seq // ws
     send = x.contiguous().view(ws, s_local, h_local, dim)
+    _shapes_agree(send)
     recv = torch.empty_like(send)
     tdist.all_to_all_single(recv, send, group=group)
     return recv.permute(1, 0, 2, 3).reshape(s_local, ws * h_local, dim)
@@ -150,6 +180,7 @@ def all_to_all_qkv(qkv: torch.Tensor, heads: int, head_dim: int
         raise RuntimeError(f"heads={heads} not divisible by world_size={ws}")
     hl = heads // ws
     send = qkv.view(s_local, 3, ws, hl, head_dim).permute(2, 0, 1, 3, 4).contiguous()
+    _shapes_agree(send)
     recv = torch.empty_like(send)
     tdist.all_to_all_single(recv, send, group=state().group)
     r = recv.view(ws * s_local, 3, hl, head_dim)
@@ -164,6 +195,7 @@ def all_gather_kv(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch
         return k, v
     st = state()
     kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
+    _shapes_agree(kv)
     out = torch.empty((st.world_size * kv.shape[0],) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
     tdist.all_gather_into_tensor(out, kv, group=st.group)
     return out[:, 0], out[:, 1]
@@ -199,6 +231,8 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: 
     rank = state().rank if is_distributed() else 0
     group = state().group if is_distributed() else None
     kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
+    if ws > 1:
+        _shapes_agree(kv)
     recv = torch.empty_like(kv) if ws > 1 else None
     acc = torch.empty(s_l, heads, d, dtype=torch.float32, device=q.device)
     acc_lse = torch.empty(heads, s_l, dtype=torch.float32, device=q.device)

@@ -2,8 +2,9 @@
 all-gather of minixmax_h3_b200.ulysses reproduce the reference's layouts
 (ops/ulysses.py, runtime/dist.py) bit-for-bit, the ring scheme
 (ops/fa_h3.py:141-218) with the oracle's attention and LSE merge plugged in
-matches attention over every rank's keys, and a rank that dies is reported by
-the others as an error."""
+matches attention over every rank's keys, and the failures a rank can cause
+(it dies, it stalls past the process group's timeout, it sends a message of
+the wrong size) reach the others as errors, not hangs or aborts."""
 from __future__ import annotations
 
 import os
@@ -30,12 +31,15 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=20))
+        short = mode in ("slow_peer", "bad_size")  # these wait for the process group's timeout
+        dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=3 if short else 20))
         from minixmax_h3_b200 import dist as hdist
         from minixmax_h3_b200 import ulysses as U
         from oracle import h3_oracle as O
 
         hdist.set_state(rank, ws, group=dist.group.WORLD, backend="gloo")
+        if mode == "bad_size":
+            os.environ["H3B_CHECK_SHAPES"] = "1"
         s, h, d = 6 * ws, 2 * ws, 4
         full = torch.arange(s * h * d, dtype=torch.float32).reshape(s, h, d)
         s0, s1 = U.split_range(s)
@@ -94,6 +98,23 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
                 results.put((rank, "no error"))
             except Exception as e:  # noqa: BLE001 - any transport error is the expected outcome
                 results.put((rank, f"error:{type(e).__name__}"))
+        elif mode in ("slow_peer", "bad_size"):
+            import time
+
+            U.all_to_all_heads(local, gather_seq=True)  # a healthy step: connections are up
+            x = local
+            if rank == ws - 1:
+                if mode == "slow_peer":
+                    time.sleep(8)  # past the others' 3 s timeout
+                else:
+                    x = local[:-1].contiguous()  # one token short: a wrong message size
+            t0 = time.monotonic()
+            try:
+                U.all_to_all_heads(x, gather_seq=True)
+                results.put((rank, "no error"))
+            except Exception as e:  # noqa: BLE001 - any transport error is the expected outcome
+                results.put((rank, f"error:{type(e).__name__}:{time.monotonic() - t0:.1f}:{str(e)[:80]}"))
+            return  # the group is broken; leave without a collective teardown
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001
         results.put((rank, f"fail:{e!r}"))
@@ -135,3 +156,28 @@ def test_dead_peer_is_reported_not_hung():
     res = _run(2, "dead_peer")
     assert res[1] == "exited"
     assert res[0].startswith("error:"), res
+
+
+def _error(msg: str) -> tuple[str, float, str]:
+    _, kind, secs, text = msg.split(":", 3)
+    return kind, float(secs), text
+
+
+def test_slow_peer_times_out_cleanly():
+    """A rank that stalls past the process group's timeout (3 s here): the
+    waiting rank gets an error after about that long instead of hanging, and
+    the late rank gets one as soon as it arrives."""
+    res = _run(2, "slow_peer")
+    assert res[0].startswith("error:") and res[1].startswith("error:"), res
+    _, secs, _ = _error(res[0])
+    assert 2.5 <= secs <= 10, res
+
+
+def test_wrong_message_size_is_a_clean_error():
+    """One rank sends a sequence slice one token short.  Unchecked, gloo would
+    abort the receiving process; with H3B_CHECK_SHAPES=1 every rank raises
+    the same RuntimeError before the exchange."""
+    res = _run(2, "bad_size")
+    for r in (0, 1):
+        kind, secs, text = _error(res[r])
+        assert kind == "RuntimeError" and "exchange mismatch" in text and secs < 2.5, res
