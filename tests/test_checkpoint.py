@@ -100,6 +100,34 @@ def test_load_dit_step(tmp_path):
         assert torch.equal(quant2[prefix]["weight"], d["weight"])
 
 
+def test_pre_quant_scale_round_trip(tmp_path):
+    """A per-input-channel pre_quant_scale stored beside a quantised weight
+    (load/safetensors_quant.py:65-78 passes it to set_quant) is adopted by
+    that layer only, and exported again."""
+    from minixmax_h3_b200 import checkpoint as ck
+
+    dense, quant = _synthetic()
+    g = torch.Generator().manual_seed(5)
+    scaled = {"blocks.0.mlp.fc2": 512, "blocks.1.attn.out_proj": 256}  # INT8 ConvRot, NVFP4
+    for prefix, k in scaled.items():
+        quant[prefix]["pre_quant_scale"] = 0.5 + torch.rand(k, generator=g)
+    path = tmp_path / "pqs.safetensors"
+    ck.save_checkpoint(path, dense, quant)
+    model = _step()
+    missing, unexpected = ck.load_checkpoint(model, path)
+    assert missing == [] and unexpected == []
+    for prefix in quant:
+        got = model.get_submodule(prefix).pre_quant_scale
+        if prefix in scaled:
+            assert torch.equal(got, quant[prefix]["pre_quant_scale"])
+        else:
+            assert got is None, prefix
+    _, quant2 = ck.export_checkpoint(model)
+    for prefix in scaled:
+        assert torch.equal(quant2[prefix]["pre_quant_scale"], quant[prefix]["pre_quant_scale"])
+    assert all("pre_quant_scale" not in quant2[p] for p in quant if p not in scaled)
+
+
 def test_load_one_block_by_prefix_and_wrapper(tmp_path):
     from minixmax_h3_b200 import checkpoint as ck
     from minixmax_h3_b200.block import DiTBlock
