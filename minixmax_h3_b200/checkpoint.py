@@ -124,6 +124,23 @@ def load_checkpoint(model: nn.Module, path: str | Path, *, device: Optional[torc
     return missing, list(unexpected)
 
 
+def load_nvfp4_linear_smoke(path: str | Path, layer_prefix: str = "model.layers.0.mlp.gate_proj", *,
+                            device: Optional[torch.device] = None,
+                            dtype: torch.dtype = torch.bfloat16) -> QuantLinear:
+    """One quantised linear of a checkpoint as a ``QuantLinear``
+    (load/safetensors_quant.py:218-240, same name and arguments): whatever
+    format its metadata names, with its scales, bias and pre_quant_scale.
+    Raises ``KeyError`` when the file has no quant metadata for the prefix."""
+    tensors, metas = load_comfy_tensors(path)
+    if layer_prefix not in metas:
+        raise KeyError(f"{layer_prefix} not in quant metas")
+    return QuantLinear.from_quant_tensors(
+        tensors[f"{layer_prefix}.weight"], meta=metas[layer_prefix],
+        weight_scale=tensors.get(f"{layer_prefix}.weight_scale"),
+        weight_scale_2=tensors.get(f"{layer_prefix}.weight_scale_2"), bias=tensors.get(f"{layer_prefix}.bias"),
+        pre_quant_scale=tensors.get(f"{layer_prefix}.pre_quant_scale"), device=device, compute_dtype=dtype)
+
+
 def save_checkpoint(path: str | Path, dense: dict[str, torch.Tensor],
                     quant: dict[str, dict[str, Any]]) -> None:
     """Write a Comfy-quant safetensors file: ``dense`` state-dict entries plus,

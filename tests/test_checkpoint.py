@@ -128,6 +128,26 @@ def test_pre_quant_scale_round_trip(tmp_path):
     assert all("pre_quant_scale" not in quant2[p] for p in quant if p not in scaled)
 
 
+def test_load_single_linear(tmp_path):
+    """load_nvfp4_linear_smoke (load/safetensors_quant.py:218-240): one layer
+    of a file, any format, with its optional tensors; unknown prefixes raise."""
+    from minixmax_h3_b200 import checkpoint as ck
+
+    dense, quant = _synthetic()
+    quant["blocks.1.mlp.fc1"]["pre_quant_scale"] = torch.full((256,), 0.75)
+    path = tmp_path / "dit.safetensors"
+    ck.save_checkpoint(path, dense, quant)
+    nv = ck.load_nvfp4_linear_smoke(path, "blocks.1.mlp.fc1", device="cpu")
+    assert nv.quant_format == "nvfp4" and (nv.out_features, nv.in_features) == (512, 256)
+    assert torch.equal(nv.weight_u8, quant["blocks.1.mlp.fc1"]["weight"])
+    assert torch.equal(nv.pre_quant_scale, quant["blocks.1.mlp.fc1"]["pre_quant_scale"])
+    i8 = ck.load_nvfp4_linear_smoke(path, "blocks.0.attn.qkv_proj", device="cpu")
+    assert i8.quant_format == "int8_tensorwise" and i8.convrot and i8.pre_quant_scale is None
+    assert torch.equal(i8.weight_i8, quant["blocks.0.attn.qkv_proj"]["weight"])
+    with pytest.raises(KeyError):
+        ck.load_nvfp4_linear_smoke(path, "blocks.0.norm1", device="cpu")
+
+
 def test_load_one_block_by_prefix_and_wrapper(tmp_path):
     from minixmax_h3_b200 import checkpoint as ck
     from minixmax_h3_b200.block import DiTBlock
