@@ -2,7 +2,6 @@
 declares, and rejects bad arguments on the host without touching a GPU."""
 from __future__ import annotations
 
-import ctypes
 import re
 from pathlib import Path
 
