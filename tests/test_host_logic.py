@@ -112,3 +112,21 @@ def test_ring_attention_single_process_is_one_merge_step():
     want, _ = O.attention_lse_fp32(q, k, v)
     assert calls == [(True, True)]
     assert torch.equal(got, want.to(torch.bfloat16))
+
+
+def test_no_alloc_gpu_tests_are_collected_last():
+    """The allocation-free entry point's GPU tests run after every other GPU
+    test, so a run that stops at the first failure has already run the
+    rest: no test file may sort after tests/test_zz_no_alloc.py."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    out = subprocess.run([sys.executable, "-m", "pytest", "tests", "--collect-only", "-q", "-m", "gpu"],
+                         capture_output=True, text=True, timeout=300, cwd=root)
+    ids = [ln for ln in out.stdout.splitlines() if "::" in ln]
+    assert ids, out.stdout[-2000:] + out.stderr[-2000:]
+    files = [i.split("::")[0] for i in ids]
+    first = files.index("tests/test_zz_no_alloc.py")
+    assert set(files[first:]) == {"tests/test_zz_no_alloc.py"}, files[first:]
