@@ -350,6 +350,22 @@ def timestep_embedding(t: torch.Tensor, dim: int = 256, max_period: float = 1000
     return torch.cat([torch.cos(a), torch.sin(a)], dim=-1)
 
 
+def curve_t_embedding(adaln_t_table: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+    """The timestep embedding of the production checkpoints (model/dit.py:
+    870-874): each t in [0, 1] (clamped) lands at position t * (grid - 1) of
+    the learned [grid, t_dim] ``adaln_t_table`` (grid 1025, t_dim 8) and is
+    the linear interpolation of the two rows around it, in fp32.  Its rows
+    feed DiTBlocks built as the checkpoints' are: t_dim 8, apply_silu=False,
+    fp16 adaLN weights (model/dit.py:655-659)."""
+    grid = adaln_t_table.shape[0]
+    if adaln_t_table.dim() != 2 or grid < 2:
+        raise ValueError("adaln_t_table must be [grid >= 2, t_dim]")
+    table = adaln_t_table.to(device=t.device, dtype=torch.float32)
+    pos = t.to(torch.float32).reshape(-1).clamp(0.0, 1.0) * (grid - 1)
+    lo = pos.floor().long().clamp(max=grid - 2)
+    return torch.lerp(table[lo], table[lo + 1], (pos - lo).unsqueeze(1))
+
+
 def quantize_linear_weight(w: torch.Tensor, fmt: str) -> dict:
     """Checkpoint-format tensors for a dense [N, K] weight (harness for random
     weights; real checkpoints arrive quantised): int8_tensorwise = symmetric

@@ -130,3 +130,25 @@ def test_no_alloc_gpu_tests_are_collected_last():
     files = [i.split("::")[0] for i in ids]
     first = files.index("tests/test_zz_no_alloc.py")
     assert set(files[first:]) == {"tests/test_zz_no_alloc.py"}, files[first:]
+
+
+def test_curve_t_embedding_interpolates_the_table():
+    """model/dit.py:870-874: t in [0, 1] -> linear interpolation between the
+    two table rows around t * (grid - 1); t = 1 gives the last row exactly and
+    values outside [0, 1] are clamped.  Checked against fp64 arithmetic."""
+    from minixmax_h3_b200.block import curve_t_embedding
+
+    g = torch.Generator().manual_seed(2)
+    table = torch.randn(1025, 8, generator=g)
+    t = torch.tensor([0.0, 1.0, 0.5, 1 / 1024, 0.3, 0.999, -0.2, 1.7])
+    got = curve_t_embedding(table, t)
+    assert got.shape == (8, 8) and got.dtype == torch.float32
+    pos = t.double().clamp(0, 1) * 1024
+    lo = pos.floor().long().clamp(max=1023)
+    frac = (pos - lo).unsqueeze(1)
+    want = table.double()[lo] * (1 - frac) + table.double()[lo + 1] * frac
+    assert torch.allclose(got.double(), want, rtol=0, atol=1e-6)
+    assert torch.equal(got[1], table[-1]) and torch.equal(got[0], table[0])
+    assert torch.equal(got[6], table[0]) and torch.equal(got[7], table[-1])
+    with pytest.raises(ValueError):
+        curve_t_embedding(torch.zeros(1, 8), t)
