@@ -98,6 +98,50 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
                 results.put((rank, "no error"))
             except Exception as e:  # noqa: BLE001 - any transport error is the expected outcome
                 results.put((rank, f"error:{type(e).__name__}"))
+        elif mode == "bnsd_entries":
+            # the reference's BNSD sequence-parallel entries, with the oracle's
+            # fp32 attention and LSE merge standing in for the two kernels
+            from minixmax_h3_b200 import attention as A
+            from minixmax_h3_b200 import ops
+
+            def fake_attention(q_, k_, v_, *, scale=None, out=None, lse=None, amax_out=None):
+                o, l_ = O.attention_lse_fp32(q_, k_, v_, scale)
+                out = torch.empty(q_.shape, dtype=torch.bfloat16) if out is None else out
+                out.copy_(o.to(torch.bfloat16))
+                if lse is not None:
+                    lse.copy_(l_)
+                return out
+
+            def fake_merge(acc, acc_lse, blk, blk_lse, *, first, out=None, amax_out=None):
+                if first:
+                    acc.copy_(blk.float())
+                    acc_lse.copy_(blk_lse)
+                else:
+                    o, l_ = O.merge_lse(acc, acc_lse, blk, blk_lse)
+                    acc.copy_(o)
+                    acc_lse.copy_(l_)
+                if out is not None:
+                    out.copy_(acc.to(torch.bfloat16))
+
+            ops.attention, ops.attention_merge_lse = fake_attention, fake_merge
+            g = torch.Generator().manual_seed(11)
+            qf, kf, vf = (torch.randn(s, h, 16, generator=g).to(torch.bfloat16) for _ in range(3))
+            want, _ = O.attention_lse_fp32(qf[s0:s1], kf, vf)  # local queries, every key
+            want = want.permute(1, 0, 2).unsqueeze(0)  # [1, H, S_local, D]
+
+            def bnsd(t):
+                return t[s0:s1].permute(1, 0, 2).unsqueeze(0).contiguous()
+
+            qb, kb, vb = bnsd(qf), bnsd(kf), bnsd(vf)
+            errs = {
+                "gather_fa_bnsd": A.gather_fa_bnsd(qb, kb, vb),
+                "sp_gather_fa": A.sp_gather_fa(qb[0], kb[0], vb[0]).unsqueeze(0),
+            }
+            os.environ["H3_ATTN_RING"] = "1"
+            errs["maybe_ring_attention_bnsd"] = A.maybe_ring_attention_bnsd(qb, kb, vb)
+            bad = {n: (o.shape, (o.float() - want).abs().max().item()) for n, o in errs.items()
+                   if o.shape != want.shape or (o.float() - want).abs().max().item() > 1e-2}
+            results.put((rank, "ok" if not bad else f"bnsd {bad}"))
         elif mode in ("slow_peer", "bad_size"):
             import time
 
@@ -149,6 +193,16 @@ def test_ulysses_exchanges_match_reference_layout(ws):
 @pytest.mark.parametrize("ws", [2, 3])
 def test_ring_attention_matches_full_attention(ws):
     res = _run(ws, "ring")
+    assert res == {r: "ok" for r in range(ws)}, res
+
+
+@pytest.mark.parametrize("ws", [2, 3])
+def test_bnsd_sequence_parallel_entries(ws):
+    """gather_fa_bnsd, sp_gather_fa and maybe_ring_attention_bnsd (the
+    reference's ops/gather_fa.py and ops/ring_attention.py entries): each
+    rank's queries against every rank's keys, as attention over the full
+    sequence."""
+    res = _run(ws, "bnsd_entries")
     assert res == {r: "ok" for r in range(ws)}, res
 
 
