@@ -396,3 +396,48 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
     call("h3b_gate_residual", x.data_ptr(), y.data_ptr(), m, hidden, x.stride(0), gate.data_ptr(), _gate_ld(gate),
          _ptr(row_sel), _stream(x))
     return x
+
+
+# ----------------------------------------------------------------------------- reference-named entries
+
+
+def rotate_activation(x: torch.Tensor, group_size: int) -> torch.Tensor:
+    """ops/hadamard.py:35-44: x [..., K] times the regular Hadamard matrix in
+    every group_size-column group (ConvRot's online rotation).  This build
+    rotates 256-column groups, exactly in fp64 and rounded once to x's dtype;
+    the reference's value comes from a 16-bit GEMM, which can differ from the
+    exact one by a unit in the last place.  Runs the rotating quantiser and
+    keeps its rotated rows."""
+    if group_size != 256:
+        raise NotImplementedError(f"ConvRot group size {group_size}: this build rotates 256-column groups")
+    *lead, k = x.shape
+    if k % group_size != 0:
+        raise ValueError(f"K={k} not divisible by group_size={group_size}")
+    x2 = x.reshape(-1, k)
+    out = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    quant_i8_rows(x2, convrot_group=group_size, x_rot_out=out)
+    return out.reshape(*lead, k)
+
+
+def int8_convrot_linear(x: torch.Tensor, weight_i8: torch.Tensor, weight_scale: torch.Tensor,
+                        bias: Optional[torch.Tensor] = None, *, convrot: bool = True, group_size: int = 256,
+                        out_dtype: torch.dtype = torch.bfloat16, weight_layout: str = "nk") -> torch.Tensor:
+    """ops/int8_convrot.py:114-209: y = W8A8(x) with x [..., K] cast to
+    out_dtype, optionally ConvRot-rotated, quantised per row and multiplied
+    by the [N, K] int8 weight with its per-channel scales (+ bias).
+
+    The ``nk`` layout is the only one: the reference's ``kn`` / ``nz29`` are
+    its NPU Cube packings.  The output is bf16 (the GEMM's epilogue rounds
+    once to bf16; an fp16 result would round twice), so other out_dtypes are
+    refused rather than approximated.  Non-CUDA tensors raise RuntimeError,
+    as the reference does for non-NPU ones."""
+    if weight_layout != "nk":
+        raise ValueError(f"weight_layout {weight_layout!r}: the tcgen05 GEMM reads the [N, K] int8 weight as stored")
+    if out_dtype != torch.bfloat16:
+        raise NotImplementedError(f"out_dtype {out_dtype}: the INT8 GEMM writes bf16")
+    *lead, k = x.shape
+    x2 = x.reshape(-1, k).to(out_dtype)
+    q, xs = quant_i8_rows(x2, convrot_group=group_size if convrot else 0)
+    b = bias.to(device=x.device, dtype=torch.bfloat16) if bias is not None else None
+    y = gemm_i8(q, xs, weight_i8, weight_scale.reshape(-1).to(device=x.device, dtype=torch.float32), b)
+    return y.reshape(*lead, weight_i8.shape[0])

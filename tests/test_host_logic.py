@@ -152,3 +152,50 @@ def test_curve_t_embedding_interpolates_the_table():
     assert torch.equal(got[6], table[0]) and torch.equal(got[7], table[-1])
     with pytest.raises(ValueError):
         curve_t_embedding(torch.zeros(1, 8), t)
+
+
+def test_reference_named_int8_entries(monkeypatch):
+    """ops.int8_convrot_linear / ops.rotate_activation (ops/int8_convrot.py:
+    114-209, ops/hadamard.py:35-44) hand the reference's arguments to the
+    quantiser and GEMM wrappers: leading dims flattened and restored, x cast
+    to bf16, ConvRot group passed, scales and bias converted; layouts, output
+    dtypes and group sizes this build cannot honour exactly are refused; CPU
+    tensors reach the wrappers' RuntimeError."""
+    import torch
+
+    from minixmax_h3_b200 import ops
+
+    x = torch.randn(2, 3, 512)
+    w = torch.zeros(64, 512, dtype=torch.int8)
+    ws = torch.ones(64, dtype=torch.float64)
+    with pytest.raises(RuntimeError):
+        ops.int8_convrot_linear(x, w, ws)  # CPU tensors: no fallback
+    with pytest.raises(ValueError):
+        ops.int8_convrot_linear(x, w, ws, weight_layout="kn")
+    with pytest.raises(NotImplementedError):
+        ops.int8_convrot_linear(x, w, ws, out_dtype=torch.float16)
+    with pytest.raises(NotImplementedError):
+        ops.rotate_activation(x, 128)
+
+    seen = {}
+
+    def fake_quant(x2, *, convrot_group=0, x_rot_out=None):
+        seen["quant"] = (x2.shape, x2.dtype, convrot_group)
+        if x_rot_out is not None:
+            x_rot_out.copy_(x2 * 2)
+        return torch.zeros(x2.shape, dtype=torch.int8), torch.ones(x2.shape[0])
+
+    def fake_gemm(q, xs, w_, ws_, b):
+        seen["gemm"] = (q.shape, w_ is w, ws_.dtype, None if b is None else b.dtype)
+        return torch.zeros(q.shape[0], w_.shape[0], dtype=torch.bfloat16)
+
+    monkeypatch.setattr(ops, "quant_i8_rows", fake_quant)
+    monkeypatch.setattr(ops, "gemm_i8", fake_gemm)
+    y = ops.int8_convrot_linear(x, w, ws, torch.zeros(64))
+    assert y.shape == (2, 3, 64) and y.dtype == torch.bfloat16
+    assert seen["quant"] == ((6, 512), torch.bfloat16, 256)
+    assert seen["gemm"] == ((6, 512), True, torch.float32, torch.bfloat16)
+    ops.int8_convrot_linear(x, w, ws, convrot=False)
+    assert seen["quant"][2] == 0
+    xr = torch.randn(4, 512).to(torch.bfloat16)
+    assert torch.equal(ops.rotate_activation(xr, 256), xr * 2)
