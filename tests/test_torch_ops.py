@@ -5,6 +5,8 @@ with the kernels replaced by recording stand-ins.  The kernels behind them
 are covered by the GPU parity tests of ``ops``."""
 from __future__ import annotations
 
+from typing import Optional
+
 import pytest
 import torch
 from torch._subclasses.fake_tensor import FakeTensorMode
@@ -125,3 +127,51 @@ def test_forwarding_to_ops(monkeypatch):
 
     codes, sf, gs = T._quant_nvfp4(torch.zeros(3, 16, dtype=BF16), True)
     assert codes.shape == (3, 8) and sf.shape == (4,) and gs.shape == (1,)
+
+
+def test_dispatch_mechanics_on_cpu(monkeypatch):
+    """torch.library's calling convention for these implementations (optional
+    tensors given as None, int epilogues, tuple results, fresh outputs),
+    exercised through CPU-device twins registered in a test namespace around
+    the same implementation functions, with the kernels replaced by
+    recorders."""
+
+    def fake_quant_nvfp4(x, *, hi_first):
+        m, k = x.shape
+        return ops.NVFP4Tensor(torch.zeros(m, k // 2, dtype=U8), torch.zeros(ops.sf_blocked_bytes(m, k), dtype=U8),
+                               torch.ones(1), m, k, hi_first)
+
+    def fake_gemm_nvfp4(a, w, bias, *, epilogue):
+        return torch.full((a.rows, w.rows // (2 if epilogue == ops.EPI_SWIGLU else 1)), float(a.k),
+                          dtype=BF16)
+
+    def fake_quant_i8(x, *, convrot_group=0, x_rot_out=None):
+        return torch.full(x.shape, convrot_group % 127, dtype=I8), torch.ones(x.shape[0])
+
+    monkeypatch.setattr(ops, "quant_nvfp4", fake_quant_nvfp4)
+    monkeypatch.setattr(ops, "gemm_nvfp4", fake_gemm_nvfp4)
+    monkeypatch.setattr(ops, "quant_i8_rows", fake_quant_i8)
+
+    @torch.library.custom_op("h3btest::quant_nvfp4", mutates_args=(), device_types="cpu")
+    def tq(x: torch.Tensor, hi_first: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        return T._quant_nvfp4(x, hi_first)
+
+    @torch.library.custom_op("h3btest::gemm_nvfp4", mutates_args=(), device_types="cpu")
+    def tg(a_codes: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, w_codes: torch.Tensor, w_sf: torch.Tensor,
+           w_gs: torch.Tensor, bias: Optional[torch.Tensor] = None, epilogue: int = 0) -> torch.Tensor:
+        return T._gemm_nvfp4(a_codes, a_sf, a_gs, w_codes, w_sf, w_gs, bias, epilogue)
+
+    @torch.library.custom_op("h3btest::quant_i8_rows", mutates_args=(), device_types="cpu")
+    def ti(x: torch.Tensor, convrot_group: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+        return T._quant_i8_rows(x, convrot_group)
+
+    x = torch.zeros(300, 512, dtype=BF16)
+    c, sf, gs = torch.ops.h3btest.quant_nvfp4(x, False)
+    assert (c.shape, sf.shape, gs.shape) == ((300, 256), (ops.sf_blocked_bytes(300, 512),), (1,))
+    w = (torch.zeros(384, 256, dtype=U8), torch.zeros(ops.sf_blocked_bytes(384, 512), dtype=U8), torch.ones(1))
+    y = torch.ops.h3btest.gemm_nvfp4(c, sf, gs, *w, None, ops.EPI_SWIGLU)
+    assert y.shape == (300, 192) and y.dtype == BF16 and float(y[0, 0]) == 512.0
+    y = torch.ops.h3btest.gemm_nvfp4(c, sf, gs, *w, torch.zeros(384, dtype=BF16), 0)
+    assert y.shape == (300, 384)
+    q, s = torch.ops.h3btest.quant_i8_rows(x, 256)
+    assert q.shape == (300, 512) and int(q[0, 0]) == 256 % 127 and s.shape == (300,)
