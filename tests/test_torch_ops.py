@@ -68,8 +68,9 @@ def test_fake_shapes():
 
 def test_traced_graph_holds_the_operators():
     """A function of the operators traces (on meta tensors, through the fake
-    implementations) to a graph of h3b calls, as the reference's custom op
-    is meant to (ops/gather_fa.py:195-206)."""
+    implementations) to a graph of h3b calls, by make_fx and by torch.compile
+    with fullgraph=True, as the reference's custom op is meant to
+    (ops/gather_fa.py:195-206)."""
     from torch.fx.experimental.proxy_tensor import make_fx
 
     def linear_w4a4(x, w_codes, w_sf, w_gs):
@@ -83,6 +84,9 @@ def test_traced_graph_holds_the_operators():
     called = [str(nd.target) for nd in g.graph.nodes if nd.op == "call_function"]
     assert "h3b.quant_nvfp4.default" in called and "h3b.gemm_nvfp4.default" in called
     assert linear_w4a4(*args).shape == (300, 384)
+    # torch.compile captures both operators in one graph (no graph break)
+    compiled = torch.compile(linear_w4a4, backend="eager", fullgraph=True)
+    assert compiled(*args).shape == (300, 384)
 
 
 def test_forwarding_to_ops(monkeypatch):
