@@ -3,6 +3,7 @@
     python -m minixmax_h3_b200.kernel_cases attention --seq 131072 --heads 3
     python -m minixmax_h3_b200.kernel_cases gemm_nvfp4 --m 8192 --n 9216 --k 3072
     python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
+    python -m minixmax_h3_b200.kernel_cases gemm_sweep --warmup 3 --iters 20   # cfg 2 + cfg 3 shapes, M 32768
     python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8_convrot --m 32768 --k 3072
@@ -40,11 +41,30 @@ def _time(fn, warmup: int, iters: int) -> float:
     return a.elapsed_time(b) / max(iters, 1)
 
 
+SWEEP_KN = ((3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072))
+
+
+def _gemm(case: str, m: int, n: int, k: int, warmup: int, iters: int, g, dev) -> dict:
+    x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if case == "gemm_nvfp4":
+        xa, wq = ops.quant_nvfp4(x), ops.quant_nvfp4(w)
+        ms = _time(lambda: ops.gemm_nvfp4(xa, wq, out=out), warmup, iters)
+    else:
+        q, xs = ops.quant_i8_rows(x)
+        wq = torch.randint(-128, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+        ws = torch.rand(n, device=dev, generator=g) * 1e-3
+        ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, out=out), warmup, iters)
+    flops = 2.0 * m * n * k
+    return {"m": m, "n": n, "k": k, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8",
                                        "quant_i8_convrot", "qk_rope", "rmsnorm_modulate", "rmsnorm_modulate_quant_i8",
-                                       "rmsnorm_modulate_quant_i8_convrot"])
+                                       "rmsnorm_modulate_quant_i8_convrot", "gemm_sweep"])
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--heads", type=int, default=24)
     ap.add_argument("--m", type=int, default=8192)
@@ -63,20 +83,14 @@ def main() -> None:
         flops = 4.0 * a.seq * a.seq * 128 * a.heads
         rec.update(seq=a.seq, heads=a.heads, ms=ms, tflops=flops / ms / 1e9, flops=flops)
     elif a.case in ("gemm_nvfp4", "gemm_i8"):
-        x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
-        w = (torch.randn(a.n, a.k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        if a.case == "gemm_nvfp4":
-            xa, wq = ops.quant_nvfp4(x), ops.quant_nvfp4(w)
-            out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device=dev)
-            ms = _time(lambda: ops.gemm_nvfp4(xa, wq, out=out), a.warmup, a.iters)
-        else:
-            q, xs = ops.quant_i8_rows(x)
-            wq = torch.randint(-128, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g)
-            ws = torch.rand(a.n, device=dev, generator=g) * 1e-3
-            out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device=dev)
-            ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, out=out), a.warmup, a.iters)
-        flops = 2.0 * a.m * a.n * a.k
-        rec.update(m=a.m, n=a.n, k=a.k, ms=ms, tflops=flops / ms / 1e9, flops=flops)
+        rec.update(_gemm(a.case, a.m, a.n, a.k, a.warmup, a.iters, g, dev))
+    elif a.case == "gemm_sweep":
+        # BASELINE cfg 2 / cfg 3: M = 32768 tokens, (K, N) of the four projections
+        m = a.m if a.m != ap.get_default("m") else 32768
+        for case in ("gemm_i8", "gemm_nvfp4"):
+            for k, n in SWEEP_KN:
+                print(json.dumps({"case": case, **_gemm(case, m, n, k, a.warmup, a.iters, g, dev)}), flush=True)
+        return
     elif a.case == "qk_rope":
         # q and k views of a packed [S, 3, H, 128] QKV buffer, in place
         from .block import RopeSpec
