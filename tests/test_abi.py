@@ -22,6 +22,18 @@ def test_header_and_binding_agree():
     assert sorted(names) == sorted(_lib.SIGNATURES)
 
 
+def test_binding_argument_counts_match_the_header():
+    """Each ctypes signature has as many arguments as the C declaration
+    (a wrong count would pass garbage across the ABI without an error)."""
+    text = HEADER.read_text()
+    found = list(re.finditer(r"H3B_API\s+int\s+(h3b_\w+)\s*\(([^;]*?)\)\s*;", text, re.S))
+    assert len(found) == len(declared())
+    for m in found:
+        name, params = m.group(1), " ".join(m.group(2).split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(_lib.SIGNATURES[name]) == n, (name, n, len(_lib.SIGNATURES[name]))
+
+
 def test_library_exports_every_symbol():
     lib = _lib.lib()
     for name in declared():
