@@ -338,8 +338,10 @@ H3B_API int h3b_attention_merge_lse(float* acc, float* acc_lse, const void* blk,
  * array (16 MiB + 256 bytes) is resident on every GPU that loads the
  * library until the process exits; all calls on a device share it, so calls
  * that overlap on the GPU race.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call
- * before any stream capture.
+ * array's device address (cudaGetSymbolAddress) and caches it; make that
+ * first call before any stream capture, and do not use the entry point
+ * across a cudaDeviceReset.  Every argument is validated before any work is
+ * queued: a rejected call leaves the array untouched.
  */
 H3B_API int h3b_rmsnorm_modulate_quant_nvfp4_noalloc(const void* x, int64_t m, int64_t hidden, int64_t ld,
                                                      const void* w, const void* shift, const void* scale,

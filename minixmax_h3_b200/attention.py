@@ -6,12 +6,10 @@
 strides in place.  There is one backend and no SDPA fallback: unsupported
 inputs raise.  The reference's sequence-parallel entries are here too:
 ``gather_fa_bnsd`` / ``sp_gather_fa`` (K/V all-gathered, then attention) and
-``ring_attention_bnsd`` / ``maybe_ring_attention_bnsd`` (the K/V ring, the
-latter gated by ``H3_ATTN_RING=1`` as in the reference).
+``ring_attention_bnsd`` (the K/V ring with log-sum-exp merges).
 """
 from __future__ import annotations
 
-import os
 from typing import Optional
 
 import torch
@@ -31,7 +29,6 @@ def fusion_attention_bnsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     kt = k[0].permute(1, 0, 2)
     vt = v[0].permute(1, 0, 2)
     if kt.stride() != vt.stride():
-        vt = vt.contiguous() if vt.is_contiguous() else vt
         kt, vt = kt.contiguous(), vt.contiguous()
     out = torch.empty((1, q.shape[1], q.shape[2], d), dtype=torch.bfloat16, device=q.device)
     ops.attention(qt, kt, vt, scale=scale, out=out[0].permute(1, 0, 2))
@@ -99,18 +96,3 @@ def ring_attention_bnsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         return fusion_attention_bnsd(q, k, v, scale=scale)
     o = ring_attention(_tokens(q), _tokens(k), _tokens(v), scale=scale)
     return o.permute(1, 0, 2).unsqueeze(0).contiguous()
-
-
-ring_attention_bnsd_fused = ring_attention_bnsd  # ops/ring_attention.py:126-192: same result, kernel path
-
-
-def maybe_ring_attention_bnsd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
-                              scale: Optional[float] = None) -> torch.Tensor:
-    """ops/ring_attention.py:195-200: the ring when ``H3_ATTN_RING=1`` and a
-    process group is up, else attention over the keys given."""
-    from .dist import is_distributed
-
-    if os.environ.get("H3_ATTN_RING", "0") == "1" and is_distributed():
-        return ring_attention_bnsd_fused(q, k, v, scale=scale)
-    return fusion_attention_bnsd(q, k, v, scale=scale)
-

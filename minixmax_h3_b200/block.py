@@ -30,8 +30,8 @@ from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantizedRows, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
-from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, clip_mod_segments, peer_buffer,
-                      phase_barrier, ring_attention, split_range, transport)
+from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, check_scheme, clip_mod_segments,
+                      peer_buffer, phase_barrier, ring_attention, split_range)
 
 
 @dataclass
@@ -136,8 +136,13 @@ ATTN_TIMER = KernelTimer()
 
 
 class Attention(nn.Module):
+    """model/dit.py:156-289.  Under a process group (``sequence_parallel``)
+    the attention runs Ulysses-sharded with the exchange scheme
+    ``seq_parallel`` (one of ``ulysses.SCHEMES``: "p2p" fused P2P stores,
+    "nccl" all-to-alls, "allgather" K/V gather, "ring" K/V ring)."""
+
     def __init__(self, hidden, heads, head_dim, eps, dtype=None, device=None, operations=None,
-                 sequence_parallel=True):
+                 sequence_parallel=True, seq_parallel: str = "p2p"):
         super().__init__()
         operations = operations or Ops
         if head_dim != 128:
@@ -145,6 +150,7 @@ class Attention(nn.Module):
         self.heads = heads
         self.head_dim = head_dim
         self.sequence_parallel = sequence_parallel
+        self.seq_parallel = check_scheme(seq_parallel)
         inner = heads * head_dim
         self.qkv_proj = operations.QuantLinear(hidden, inner * 3, bias=False, dtype=dtype, device=device)
         self.q_norm = operations.RMSNorm(head_dim, eps=eps, dtype=dtype, device=device)
@@ -158,10 +164,10 @@ class Attention(nn.Module):
         otherwise returns attn(h)."""
         s_local = h.shape[0]
         sp = self.sequence_parallel and is_distributed()
-        if sp and transport() == "p2p":
+        if sp and self.seq_parallel == "p2p":
             return self._forward_p2p(h, rope_freqs, amax_h=amax_h, resid=resid, gate=gate, row_sel=row_sel)
-        gather_kv = sp and transport() == "allgather"
-        ring = sp and transport() == "ring"
+        gather_kv = sp and self.seq_parallel == "allgather"
+        ring = sp and self.seq_parallel == "ring"
         qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
         if rope_freqs is not None:
@@ -285,13 +291,14 @@ class DiTBlock(nn.Module):
     """model/dit.py:400-449 on the fused kernels."""
 
     def __init__(self, hidden, heads, head_dim, ffn, t_dim, eps, qk_eps, apply_silu=True, adaln_dtype=None,
-                 dtype=None, device=None, operations=None, mlp_act: str = "swiglu"):
+                 dtype=None, device=None, operations=None, mlp_act: str = "swiglu", seq_parallel: str = "p2p"):
         super().__init__()
         operations = operations or Ops
         self.hidden = hidden
         self.norm1 = operations.RMSNorm(hidden, eps=eps, dtype=dtype, device=device)
         self.norm2 = operations.RMSNorm(hidden, eps=eps, dtype=dtype, device=device)
-        self.attn = Attention(hidden, heads, head_dim, qk_eps, dtype=dtype, device=device, operations=operations)
+        self.attn = Attention(hidden, heads, head_dim, qk_eps, dtype=dtype, device=device, operations=operations,
+                              seq_parallel=seq_parallel)
         self.mlp = MLP(hidden, ffn, dtype=dtype, device=device, operations=operations, act=mlp_act)
         self.adaln_proj = AdalnProj(t_dim, hidden, 6, 3, apply_silu=apply_silu,
                                     dtype=adaln_dtype if adaln_dtype is not None else dtype, device=device,
@@ -411,13 +418,14 @@ class DiTStep(nn.Module):
     (model/dit.py:852-867).  Under Ulysses every rank holds S/ws tokens."""
 
     def __init__(self, *, hidden: int, heads: int, ffn: int, depth: int, text_dim: int, t_dim: int = 256,
-                 fmt: str = "nvfp4", mlp_act: str = "gelu", eps: float = 1e-6, device=None):
+                 fmt: str = "nvfp4", mlp_act: str = "gelu", eps: float = 1e-6, device=None,
+                 seq_parallel: str = "p2p"):
         super().__init__()
         self.hidden, self.t_dim = hidden, t_dim
         self.condition_proj = QuantLinear(text_dim, hidden, bias=False, device=device)
         self.blocks = nn.ModuleList([
             DiTBlock(hidden, heads, 128, ffn, t_dim, eps, eps, apply_silu=True, dtype=torch.bfloat16,
-                     device=device, mlp_act=mlp_act) for _ in range(depth)])
+                     device=device, mlp_act=mlp_act, seq_parallel=seq_parallel) for _ in range(depth)])
         self.fmt = fmt
 
     def init_random(self, seed: int = 0) -> None:

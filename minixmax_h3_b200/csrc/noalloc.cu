@@ -16,7 +16,10 @@
 // library and stays there until the process exits.  All calls on a device
 // share it and it keeps the last call's contents; the |h| max is cleared at
 // the start of every call.  Two calls that overlap on the GPU (on different
-// streams, without ordering between them) race on it.
+// streams, without ordering between them) race on it.  The array's device
+// address is looked up once per device and cached, so the entry point must
+// not be used across a cudaDeviceReset of that device (the reset unloads the
+// module and the cached address would dangle).
 #include <cstdint>
 #include <mutex>
 
@@ -59,10 +62,18 @@ extern "C" int h3b_rmsnorm_modulate_quant_nvfp4_noalloc(const void* x, int64_t m
                                                         int64_t tab_ld, const int32_t* row_sel, float eps,
                                                         uint8_t* codes, uint8_t* sf, float* gs_out, int hi_first,
                                                         h3b_stream_t stream) {
-  if (m <= 0 || hidden <= 0 || (hidden % 64) != 0 || ld < hidden) return H3B_ERR_SHAPE;
+  // Every check of both callees runs here first, so a rejected call queues
+  // nothing and leaves the shared array as it was.
+  if (x == nullptr || w == nullptr || shift == nullptr || scale == nullptr || codes == nullptr || sf == nullptr ||
+      gs_out == nullptr)
+    return H3B_ERR_ARG;
+  if (m <= 0 || hidden <= 0 || (hidden % 64) != 0 || ld < hidden || (ld % 8) != 0) return H3B_ERR_SHAPE;
   // h is held with the row stride of x: reject what does not fit the array
   if (ld > static_cast<int64_t>(kRowsBytes / 2) || m > static_cast<int64_t>(kRowsBytes / 2) / ld)
     return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(x) || !h3b::aligned16(w) || !h3b::aligned16(shift) || !h3b::aligned16(scale) ||
+      !h3b::aligned16(codes) || (reinterpret_cast<uintptr_t>(sf) & 3u) != 0 || tab_ld < 0 || (tab_ld % 8) != 0)
+    return H3B_ERR_ALIGN;
   void* base = nullptr;
   int rc = scratch_address(&base);
   if (rc != H3B_OK) return rc;

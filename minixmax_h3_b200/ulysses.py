@@ -3,29 +3,30 @@
 Same contract as the reference's ops/ulysses.py:14-61: every rank holds
 S/ws tokens with all heads for the projections, and all S tokens with H/ws
 heads (rank r owns heads [r*H/ws, (r+1)*H/ws)) for attention; the sequence
-order after the exchange is the rank order.  Three sequence-parallel
-schemes (``H3B_ULYSSES``):
+order after the exchange is the rank order.  The sequence-parallel scheme is
+an explicit argument (``SCHEMES``; ``block.Attention(seq_parallel=...)``):
 
+* ``p2p`` (default): no separate exchange.  The QKV GEMM epilogue stores
+  each output block straight into the head owner's receive buffer, and the
+  attention epilogue stores each output row into the token owner's
+  out-projection input, through buffers mapped by CUDA IPC
+  (``PeerBuffer``).  A collective on the compute stream orders each phase.
 * ``nccl``: NCCL ``all_to_all_single`` over NVLink.  ``all_to_all_qkv``
   moves the packed [S_local, 3, H, D] projection output in ONE exchange and
   returns q/k/v as strided views that the attention kernel reads in place.
-* ``p2p`` (default with CUDA): no separate exchange.  The QKV GEMM epilogue
-  stores each output block straight into the head owner's receive buffer,
-  and the attention epilogue stores each output row into the token owner's
-  out-projection input, through buffers mapped by CUDA IPC
-  (``PeerBuffer``).  A collective on the compute stream orders each phase.
 * ``allgather``: the reference's production scheme (model/dit.py:200-248):
   no head exchange; K and V of all tokens are gathered once
   (``all_gather_kv``, runtime/dist.py:291-312) and every rank attends its
   own queries over all keys, all heads.
+* ``ring``: K/V chunks travel around the ring and the chunk results merge
+  through their log-sum-exps (``ring_attention``, ops/fa_h3.py:159-218).
 
-``H3B_CHECK_SHAPES=1`` makes every exchange first confirm that all ranks send
-messages of one shape (``_shapes_agree``).
+``check_shapes=True`` on an exchange makes it first confirm that all ranks
+send messages of one shape (``_shapes_agree``).
 """
 from __future__ import annotations
 
 import ctypes
-import os
 from typing import Optional, Sequence
 
 import torch
@@ -36,13 +37,14 @@ from ._lib import call
 from .dist import is_distributed, state
 
 
-def transport() -> str:
-    """"p2p" (fused P2P stores, default), "nccl", "allgather" or "ring"
-    (H3B_ULYSSES)."""
-    t = os.environ.get("H3B_ULYSSES", "p2p")
-    if t not in ("p2p", "nccl", "allgather", "ring"):
-        raise ValueError(f"H3B_ULYSSES={t!r}: expected p2p, nccl, allgather or ring")
-    return t
+SCHEMES = ("p2p", "nccl", "allgather", "ring")
+
+
+def check_scheme(scheme: str) -> str:
+    """Validates a sequence-parallel scheme name (one of ``SCHEMES``)."""
+    if scheme not in SCHEMES:
+        raise ValueError(f"seq_parallel={scheme!r}: expected one of {', '.join(SCHEMES)}")
+    return scheme
 
 
 class PeerBuffer:
@@ -111,14 +113,14 @@ def phase_barrier(device: torch.device, flag: Optional[torch.Tensor] = None) -> 
     tdist.all_reduce(flag, op=tdist.ReduceOp.MAX, group=state().group)
 
 
-def _shapes_agree(t: torch.Tensor) -> None:
-    """With ``H3B_CHECK_SHAPES=1``: before an exchange, every rank's message
-    (shape and element size) must match, else every rank raises the same
-    RuntimeError.  Without the check a mismatch is not a clean error: gloo
-    aborts the receiving process (its pair size check ends in
-    std::terminate) and NCCL moves the wrong bytes.  Costs one small
-    all_gather per exchange, so it is off by default."""
-    if os.environ.get("H3B_CHECK_SHAPES", "0") != "1":
+def _shapes_agree(t: torch.Tensor, check: bool) -> None:
+    """With ``check``: before an exchange, every rank's message (shape and
+    element size) must match, else every rank raises the same RuntimeError.
+    Without the check a mismatch is not a clean error: gloo aborts the
+    receiving process (its pair size check ends in std::terminate) and NCCL
+    moves the wrong bytes.  Costs one small all_gather per exchange, so the
+    exchanges default to check=False."""
+    if not check:
         return
     st = state()
     dims = list(t.shape)
@@ -136,7 +138,7 @@ def _shapes_agree(t: torch.Tensor) -> None:
             raise RuntimeError(f"exchange mismatch: rank 0 sends {desc(rows[0])}, rank {r} sends {desc(row)}")
 
 
-def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
+def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool, check_shapes: bool = False) -> torch.Tensor:
     """gather_seq=True: [S_local, H, D] -> [S, H/ws, D];
     gather_seq=False: [S, H/ws, D] -> [S_local, H, D]  (ops/ulysses.py:14-41)."""
     if not is_distributed():
@@ -149,7 +151,7 @@ def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
             raise RuntimeError(f"heads={heads} not divisible by world_size={ws}")
         h_local = heads // ws
         send = x.view(s_local, ws, h_local, dim).permute(1, 0, 2, 3).contiguous()
-        _shapes_agree(send)
+        _shapes_agree(send, check_shapes)
         recv = torch.empty_like(send)
         tdist.all_to_all_single(recv, send, group=group)
         return recv.reshape(ws * s_local, h_local, dim)
@@ -158,13 +160,13 @@ def all_to_all_heads(x: torch.Tensor, *, gather_seq: bool) -> torch.Tensor:
         raise RuntimeError(f"seq={seq} not divisible by world_size={ws}")
     s_local = seq // ws
     send = x.contiguous().view(ws, s_local, h_local, dim)
-    _shapes_agree(send)
+    _shapes_agree(send, check_shapes)
     recv = torch.empty_like(send)
     tdist.all_to_all_single(recv, send, group=group)
     return recv.permute(1, 0, 2, 3).reshape(s_local, ws * h_local, dim)
 
 
-def all_to_all_qkv(qkv: torch.Tensor, heads: int, head_dim: int
+def all_to_all_qkv(qkv: torch.Tensor, heads: int, head_dim: int, *, check_shapes: bool = False
                    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Packed seq->head exchange of a [S_local, 3*H*D] projection output.
 
@@ -180,14 +182,15 @@ def all_to_all_qkv(qkv: torch.Tensor, heads: int, head_dim: int
         raise RuntimeError(f"heads={heads} not divisible by world_size={ws}")
     hl = heads // ws
     send = qkv.view(s_local, 3, ws, hl, head_dim).permute(2, 0, 1, 3, 4).contiguous()
-    _shapes_agree(send)
+    _shapes_agree(send, check_shapes)
     recv = torch.empty_like(send)
     tdist.all_to_all_single(recv, send, group=state().group)
     r = recv.view(ws * s_local, 3, hl, head_dim)
     return r[:, 0], r[:, 1], r[:, 2]
 
 
-def all_gather_kv(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+def all_gather_kv(k: torch.Tensor, v: torch.Tensor, *, check_shapes: bool = False
+                  ) -> tuple[torch.Tensor, torch.Tensor]:
     """[S_local, H, D] k and v of every rank -> [S, H, D] views of one gathered
     buffer, rank order = sequence order (runtime/dist.py:291-312 with
     seq_dim=0: one collective for K and V together)."""
@@ -195,7 +198,7 @@ def all_gather_kv(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch
         return k, v
     st = state()
     kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
-    _shapes_agree(kv)
+    _shapes_agree(kv, check_shapes)
     out = torch.empty((st.world_size * kv.shape[0],) + tuple(kv.shape[1:]), dtype=kv.dtype, device=kv.device)
     tdist.all_gather_into_tensor(out, kv, group=st.group)
     return out[:, 0], out[:, 1]
@@ -207,7 +210,7 @@ def _global_rank(group, r: int) -> int:
 
 def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: Optional[float] = None,
                    out: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
-                   attention_fn=None, merge_fn=None) -> torch.Tensor:
+                   attention_fn=None, merge_fn=None, check_shapes: bool = False) -> torch.Tensor:
     """Ring sequence parallelism (ops/fa_h3.py:159-218, ring_attention_lse_bnsd):
     this rank's queries q [S_local, H, D] attend to every rank's keys/values,
     which travel around the ring (rank r sends to r+1 and receives from r-1)
@@ -232,7 +235,7 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: 
     group = state().group if is_distributed() else None
     kv = torch.stack((k, v), dim=1).contiguous()  # [S_local, 2, H, D]
     if ws > 1:
-        _shapes_agree(kv)
+        _shapes_agree(kv, check_shapes)
     recv = torch.empty_like(kv) if ws > 1 else None
     acc = torch.empty(s_l, heads, d, dtype=torch.float32, device=q.device)
     acc_lse = torch.empty(heads, s_l, dtype=torch.float32, device=q.device)

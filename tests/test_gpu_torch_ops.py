@@ -1,6 +1,6 @@
 """GPU: the ``torch.ops.h3b.*`` operators and the reference-named entries
 (ops.int8_convrot_linear / rotate_activation, attention.gather_fa_bnsd /
-sp_gather_fa / ring_attention_bnsd / maybe_ring_attention_bnsd) give the same
+sp_gather_fa / ring_attention_bnsd) give the same
 bits as the ``ops`` calls and entries they wrap: the same kernels on the same
 inputs, so the comparison is exact."""
 from __future__ import annotations
@@ -92,4 +92,3 @@ def test_reference_named_entries(cuda):
     assert torch.equal(A.gather_fa_bnsd(q, k, v), want)
     assert torch.equal(A.sp_gather_fa(q[0], k[0], v[0]), want[0])
     assert torch.equal(A.ring_attention_bnsd(q, k, v), want)
-    assert torch.equal(A.maybe_ring_attention_bnsd(q, k, v), want)

@@ -40,7 +40,7 @@ def _free_port() -> int:
 def _worker(rank: int, ws: int, port: int, fmt: str, transport: str, mlp_act: str, out_q) -> None:
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(ws),
-                      LOCAL_RANK=str(rank), H3B_ULYSSES=transport)
+                      LOCAL_RANK=str(rank))
     import torch.distributed as tdist
 
     from minixmax_h3_b200 import dist as hdist
@@ -52,7 +52,7 @@ def _worker(rank: int, ws: int, port: int, fmt: str, transport: str, mlp_act: st
         dev = torch.device("cuda", rank)
         hidden, heads = 512, 4
         blk = DiTBlock(hidden, heads, 128, 4 * hidden, 256, 1e-6, 1e-6, dtype=torch.bfloat16, device=dev,
-                       mlp_act=mlp_act)
+                       mlp_act=mlp_act, seq_parallel=transport)
         init_block_random(blk, fmt, torch.Generator(device=dev).manual_seed(0))  # same on every rank
         pos = RopeSpec.grid_positions(4, 16, 24)
         rope = RopeSpec.build(pos, device=dev)

@@ -38,8 +38,7 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
         from oracle import h3_oracle as O
 
         hdist.set_state(rank, ws, group=dist.group.WORLD, backend="gloo")
-        if mode == "bad_size":
-            os.environ["H3B_CHECK_SHAPES"] = "1"
+        check = mode == "bad_size"  # exchanges confirm the message shapes first
         s, h, d = 6 * ws, 2 * ws, 4
         full = torch.arange(s * h * d, dtype=torch.float32).reshape(s, h, d)
         s0, s1 = U.split_range(s)
@@ -87,7 +86,7 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
             err = (got.float() - want).abs().max().item()
             results.put((rank, "ok" if err < 1e-2 else f"ring err {err}"))
         elif mode == "dead_peer":
-            U.all_to_all_heads(local, gather_seq=True)  # a healthy step: connections are up
+            U.all_to_all_heads(local, gather_seq=True, check_shapes=check)  # a healthy step: connections are up
             if rank == ws - 1:
                 results.put((rank, "exited"))
                 results.close()
@@ -137,15 +136,14 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
                 "gather_fa_bnsd": A.gather_fa_bnsd(qb, kb, vb),
                 "sp_gather_fa": A.sp_gather_fa(qb[0], kb[0], vb[0]).unsqueeze(0),
             }
-            os.environ["H3_ATTN_RING"] = "1"
-            errs["maybe_ring_attention_bnsd"] = A.maybe_ring_attention_bnsd(qb, kb, vb)
+            errs["ring_attention_bnsd"] = A.ring_attention_bnsd(qb, kb, vb)
             bad = {n: (o.shape, (o.float() - want).abs().max().item()) for n, o in errs.items()
                    if o.shape != want.shape or (o.float() - want).abs().max().item() > 1e-2}
             results.put((rank, "ok" if not bad else f"bnsd {bad}"))
         elif mode in ("slow_peer", "bad_size"):
             import time
 
-            U.all_to_all_heads(local, gather_seq=True)  # a healthy step: connections are up
+            U.all_to_all_heads(local, gather_seq=True, check_shapes=check)  # a healthy step: connections are up
             x = local
             if rank == ws - 1:
                 if mode == "slow_peer":
@@ -154,7 +152,7 @@ def _worker(rank: int, ws: int, port: int, mode: str, results) -> None:
                     x = local[:-1].contiguous()  # one token short: a wrong message size
             t0 = time.monotonic()
             try:
-                U.all_to_all_heads(x, gather_seq=True)
+                U.all_to_all_heads(x, gather_seq=True, check_shapes=check)
                 results.put((rank, "no error"))
             except Exception as e:  # noqa: BLE001 - any transport error is the expected outcome
                 results.put((rank, f"error:{type(e).__name__}:{time.monotonic() - t0:.1f}:{str(e)[:80]}"))
@@ -198,7 +196,7 @@ def test_ring_attention_matches_full_attention(ws):
 
 @pytest.mark.parametrize("ws", [2, 3])
 def test_bnsd_sequence_parallel_entries(ws):
-    """gather_fa_bnsd, sp_gather_fa and maybe_ring_attention_bnsd (the
+    """gather_fa_bnsd, sp_gather_fa and ring_attention_bnsd (the
     reference's ops/gather_fa.py and ops/ring_attention.py entries): each
     rank's queries against every rank's keys, as attention over the full
     sequence."""
@@ -229,7 +227,7 @@ def test_slow_peer_times_out_cleanly():
 
 def test_wrong_message_size_is_a_clean_error():
     """One rank sends a sequence slice one token short.  Unchecked, gloo would
-    abort the receiving process; with H3B_CHECK_SHAPES=1 every rank raises
+    abort the receiving process; with check_shapes=True every rank raises
     the same RuntimeError before the exchange."""
     res = _run(2, "bad_size")
     for r in (0, 1):

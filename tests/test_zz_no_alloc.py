@@ -15,12 +15,15 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _inputs(seed: int, m: int, hidden: int, device):
+def _inputs(seed: int, m: int, hidden: int, device, *, gain: float = 1.0, pad: int = 0, row_sel: bool = True):
+    """x [m, hidden] (a column slice of a [m, hidden + pad] tensor when pad > 0,
+    so its row stride exceeds hidden), the norm weight and adaLN tables scaled
+    by `gain`, and per-token table rows (or None)."""
     g = torch.Generator().manual_seed(seed)
-    x = (torch.randn(m, hidden, generator=g) * 2).to(torch.bfloat16).to(device)
-    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16).to(device)
-    tab = (0.2 * torch.randn(2, 2 * hidden, generator=g)).to(torch.bfloat16).to(device)
-    sel = torch.randint(-1, 2, (m,), generator=g, dtype=torch.int32).to(device)
+    x = (torch.randn(m, hidden + pad, generator=g) * 2).to(torch.bfloat16).to(device)[:, :hidden]
+    w = (gain * (1 + 0.1 * torch.randn(hidden, generator=g))).to(torch.bfloat16).to(device)
+    tab = (gain * 0.2 * torch.randn(2, 2 * hidden, generator=g)).to(torch.bfloat16).to(device)
+    sel = torch.randint(-1, 2, (m,), generator=g, dtype=torch.int32).to(device) if row_sel else None
     return x, w, tab[:, :hidden], tab[:, hidden:], sel
 
 
@@ -33,8 +36,9 @@ def _noalloc(x, w, shift, scale, sel, hi_first):
     sf = torch.empty(ops.sf_blocked_bytes(m, hidden), dtype=torch.uint8, device=x.device)
     gs = torch.empty(1, dtype=torch.float32, device=x.device)
     call("h3b_rmsnorm_modulate_quant_nvfp4_noalloc", x.data_ptr(), m, hidden, x.stride(0), w.data_ptr(),
-         shift.data_ptr(), scale.data_ptr(), shift.stride(0), sel.data_ptr(), 1e-6, codes.data_ptr(),
-         sf.data_ptr(), gs.data_ptr(), 1 if hi_first else 0, torch.cuda.current_stream(x.device).cuda_stream)
+         shift.data_ptr(), scale.data_ptr(), shift.stride(0), None if sel is None else sel.data_ptr(), 1e-6,
+         codes.data_ptr(), sf.data_ptr(), gs.data_ptr(), 1 if hi_first else 0,
+         torch.cuda.current_stream(x.device).cuda_stream)
     return codes, sf, gs
 
 
@@ -42,17 +46,37 @@ def _two_calls(x, w, shift, scale, sel, hi_first):
     from minixmax_h3_b200 import ops
 
     amax = torch.zeros(1, dtype=torch.float32, device=x.device)
-    h = ops.rmsnorm_modulate(x, w, shift, scale, 1e-6, row_sel=sel, amax_out=amax)
+    m, hidden = x.shape
+    h = torch.empty(m, x.stride(0), dtype=torch.bfloat16, device=x.device)[:, :hidden]  # x's row stride
+    h = ops.rmsnorm_modulate(x, w, shift, scale, 1e-6, row_sel=sel, amax_out=amax, out=h)
     t = ops.quant_nvfp4(h, hi_first=hi_first, amax_t=amax)
     return t.codes, t.sf, t.gs
 
 
 def test_noalloc_matches_two_call_path(cuda):
-    for seed, (m, hidden), hi_first in ((0, (300, 3072), True), (1, (129, 1024), False)):
-        args = _inputs(seed, m, hidden, cuda)
+    """Two calls in a row.  The second call's |h| max is about ten times
+    smaller than the first's (norm weight and tables scaled by 0.1; scaling x
+    would not change h, which RMSNorm normalises), so a max left over from the
+    first call would give it a wrong global scale and wrong codes."""
+    gs_seen = []
+    for seed, (m, hidden), hi_first, gain in ((0, (300, 3072), True, 1.0), (1, (129, 1024), False, 0.1)):
+        args = _inputs(seed, m, hidden, cuda, gain=gain)
         got = _noalloc(*args, hi_first)
         want = _two_calls(*args, hi_first)
         for a, b in zip(got, want):
+            assert torch.equal(a, b)
+        gs_seen.append(got[2].item())
+    assert gs_seen[1] < 0.5 * gs_seen[0], gs_seen
+
+
+def test_noalloc_wide_row_stride_and_no_row_sel(cuda):
+    """x as a column slice of a wider tensor (row stride hidden + 64, which
+    the array holds h with) and row_sel NULL (every token on table row 0),
+    bit-exact against the two-call path."""
+    for seed, row_sel in ((3, True), (4, False)):
+        args = _inputs(seed, 200, 1024, cuda, pad=64, row_sel=row_sel)
+        assert args[0].stride(0) == 1024 + 64
+        for a, b in zip(_noalloc(*args, True), _two_calls(*args, True)):
             assert torch.equal(a, b)
 
 
