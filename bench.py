@@ -7,7 +7,9 @@ Workload (the same total sequence at every N — strong scaling):
   44/42/42, adaLN from a 256-d sinusoidal timestep embedding.  Random-init
   weights (no checkpoints offline), synthetic bf16 N(0,1) inputs; every
   activation tensor (3 GB and up) is far larger than the 126 MB L2.
-  N > 1: Ulysses sequence parallelism over NCCL, one process per GPU.
+  N > 1: Ulysses sequence parallelism, one process per GPU: the seq->head
+  and head->seq exchanges are P2P stores fused into the QKV GEMM and
+  attention epilogues, ordered by small NCCL collectives.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     (N > 1: torchrun --nproc-per-node N bench.py --gpus N ...)
@@ -41,8 +43,15 @@ GRID = (61, 68, 120)
 S_VIDEO = GRID[0] * GRID[1] * GRID[2]
 S_TOTAL = N_TEXT + S_VIDEO  # 498,272
 METRIC = "DiT-block tokens/s"
-REF_TOKENS, REF_Q_ROWS = 1024, 128  # CPU sample per reference step (~1 s of CPU work)
-ATTN_DRAM_BYTES_24_HEADS = 1.57e12 + 3.31e9  # ncu dram__bytes_read.sum + write.sum, one launch
+# CPU sample per reference step: tokens through the non-attention work and
+# query rows of one head against all keys (about 10 s of CPU work on 16 cores)
+REF_TOKENS, REF_Q_ROWS = 4096, 512
+WARM_TOKENS, WARM_Q_ROWS = 1024, 128  # untimed warm-up sample
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention
+# launch over ONE head at the bench's S = 498,272 (small-case ncu capture,
+# profiles/attention_kernel_S498272_H1_dram.md); a launch over H heads moves
+# H times that, since every wave of CTAs works on one head at a time.
+ATTN_DRAM_BYTES_PER_HEAD = None
 UNIT = "block-tokens/s"
 WORKLOAD = ("cfg5: one denoising step of 4 DiT blocks, hidden 3072, 24x128 heads, GELU MLP 12288, NVFP4 W4A4 "
             "linears, 512 text (dim 4096) + 497760 video tokens (t61 x h68 x w120) = 498272-token joint attention, "
@@ -191,7 +200,7 @@ def run_reference(args) -> None:
     torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
     cores = torch.get_num_threads()
     for _ in range(args.warmup):
-        cpu_reference_sample(REF_Q_ROWS, REF_TOKENS)
+        cpu_reference_sample(WARM_Q_ROWS, WARM_TOKENS)
     vals, secs, sample = [], 0.0, ""
     for _ in range(args.steps):
         r = cpu_reference_sample(REF_Q_ROWS, REF_TOKENS)
@@ -201,14 +210,146 @@ def run_reference(args) -> None:
     value = statistics.mean(vals)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * S_TOTAL * DEPTH / value,
+            "ms_per_step_kind": (f"extrapolated from the sample: each step timed {secs / args.steps:.1f} s of CPU "
+                                 f"work and a whole step at S={S_TOTAL} would take ms_per_step"),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (W4A16 host path)",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "seq_len": S_TOTAL, "blocks": DEPTH},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "data": "synthetic", "config": _config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "threads": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+def _config(ws: int) -> dict:
+    return {"workload": WORKLOAD, "seq_len": S_TOTAL, "blocks": DEPTH, "hidden": HIDDEN, "heads": HEADS,
+            "mlp": FFN, "parallelism": f"ulysses{ws}", "l2": "inputs larger than L2 (>= 3 GB tensors)"}
+
+
 # ----------------------------------------------------------------------------- GPU leg
+
+
+PARITY_CFG = {"hidden": 1024, "heads": 8, "ffn": 4096, "depth": 2, "text_dim": 1024, "n_text": 64,
+              "grid": (4, 16, 63)}  # 64 text + 4032 video = 4096 tokens; 8 heads shard over up to 8 ranks
+
+
+def parity_check(ws: int, rank: int, dev: torch.device) -> dict:
+    """Runs on every rank, after the timed steps.
+
+    1. Sharded vs one GPU (N > 1): a small P2P-Ulysses step (PARITY_CFG, two
+       blocks, NVFP4 and INT8 linears) runs sharded over the N ranks; rank 0
+       gathers the outputs and compares them, bit for bit, with the same step
+       run on rank 0 alone.  The NVFP4 global scales are max-reduced across
+       ranks, so the sharded step quantises exactly as the single-GPU one.
+    2. Golden (rank 0): a DiT block built from the weights of the committed
+       golden fixture tests/golden/dit_block_nvfp4_gelu.pt, which the
+       reference's own DiTBlock (model/dit.py:400-438) produced, must match the
+       fixture's output within the float bar (scaled max-abs <= 2e-2, cosine
+       >= 0.9995); the raw max-abs is reported too.
+    """
+    import torch.distributed as tdist
+
+    from minixmax_h3_b200 import dist as hdist
+    from minixmax_h3_b200.block import DiTStep, RopeSpec
+
+    c = PARITY_CFG
+    out: dict = {"n": ws}
+    text_pos = torch.stack([torch.arange(c["n_text"], dtype=torch.float32), torch.zeros(c["n_text"]),
+                            torch.zeros(c["n_text"])], -1)
+    pos = torch.cat([text_pos, RopeSpec.grid_positions(*c["grid"])])
+    s_total = pos.shape[0]
+    rope = RopeSpec.build(pos, device=dev)
+    g = torch.Generator(device=dev).manual_seed(21)
+    video = torch.randn(s_total - c["n_text"], c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    text = torch.randn(c["n_text"], c["text_dim"], generator=g, device=dev).to(torch.bfloat16)
+    ts = torch.tensor([321.0], device=dev)
+    s_local = s_total // ws
+    s0 = rank * s_local
+    n_text_here = max(0, min(c["n_text"], s0 + s_local) - s0)
+    v0 = s0 + n_text_here - c["n_text"]
+    video_local = video[v0:v0 + s_local - n_text_here]
+    exact: dict = {}
+    for fmt in ("nvfp4", "int8_tensorwise"):
+        step = DiTStep(hidden=c["hidden"], heads=c["heads"], ffn=c["ffn"], depth=c["depth"], text_dim=c["text_dim"],
+                       fmt=fmt, mlp_act="gelu", device=dev, seq_parallel="p2p")
+        step.init_random(seed=5)  # identical weights on every rank
+        with torch.no_grad():
+            y_local = step(video_local.clone(), text, ts, rope)
+            if ws > 1:
+                parts = [torch.empty_like(y_local) for _ in range(ws)]
+                tdist.all_gather(parts, y_local)
+                if rank == 0:
+                    st = hdist.state()
+                    hdist.set_state(0, 1)  # the same step on this GPU alone
+                    try:
+                        y_one = step(video.clone(), text, ts, rope)
+                    finally:
+                        hdist.set_state(st.rank, st.world_size, local_rank=st.local_rank, group=st.group,
+                                        backend=st.backend)
+                    y_sp = torch.cat(parts)
+                    exact[fmt] = bool(torch.equal(y_sp, y_one))
+                    if not exact[fmt]:
+                        d = (y_sp.float() - y_one.float()).abs()
+                        exact[f"{fmt}_max_abs"] = d.max().item()
+                tdist.barrier(device_ids=[dev.index])
+        del step
+    if ws > 1:
+        out["sharded_vs_one_gpu"] = {"exact": all(v for k, v in exact.items() if not k.endswith("_max_abs"))
+                                     if rank == 0 else None, "formats": exact, "tokens": s_total,
+                                     "hidden": c["hidden"], "heads": c["heads"], "blocks": c["depth"],
+                                     "scheme": "p2p"}
+    else:
+        out["sharded_vs_one_gpu"] = None  # one GPU: nothing is sharded
+    if rank == 0:
+        out["golden"] = _golden_block_check(dev)
+    return out
+
+
+def _golden_block_check(dev: torch.device) -> dict:
+    """The fixture's DiT block on this GPU against the reference's output."""
+    from minixmax_h3_b200 import dist as hdist
+    from minixmax_h3_b200.block import DiTBlock, RopeSpec, load_quant_linear
+    if str(ROOT / "tests") not in sys.path:
+        sys.path.insert(0, str(ROOT / "tests"))
+    from golden.fixture_params import block_fixture_params
+
+    fix = torch.load(ROOT / "tests" / "golden" / "dit_block_nvfp4_gelu.pt", weights_only=False)
+    p = block_fixture_params(fix)
+    hidden = fix["hidden"]
+    st = hdist.state()
+    hdist.set_state(0, 1)
+    try:
+        blk = DiTBlock(hidden, fix["heads"], 128, 4 * hidden, fix["t_dim"], fix["eps"], fix["qk_eps"],
+                       apply_silu=True, dtype=torch.bfloat16, device=dev, mlp_act=fix["mlp_act"])
+        for mod, name in ((blk.attn.qkv_proj, "qkv"), (blk.attn.out_proj, "out"), (blk.mlp.fc1, "fc1"),
+                          (blk.mlp.fc2, "fc2")):
+            load_quant_linear(mod, p[f"{name}_w"].to(dev), "nvfp4")
+        for mod, name in ((blk.norm1, "norm1_w"), (blk.norm2, "norm2_w"), (blk.attn.q_norm, "q_norm_w"),
+                          (blk.attn.k_norm, "k_norm_w")):
+            mod.weight.data.copy_(p[name])
+        blk.adaln_proj.linear.weight.data.copy_(p["adaln_w"])
+        blk.adaln_proj.linear.bias.data.copy_(p["adaln_b"])
+        rope = RopeSpec(fix["pos"].to(dev), fix["inv_freq"].to(dev), fix["n_t"], fix["n_h"])
+        with torch.no_grad():
+            y = blk(fix["x"].to(dev).clone(), fix["t_emb"].to(dev), fix["segments"], rope)
+    finally:
+        hdist.set_state(st.rank, st.world_size, local_rank=st.local_rank, group=st.group, backend=st.backend)
+    got, want = y.float().cpu().reshape(-1), fix["out"].float().reshape(-1)
+    diff = (got - want).abs()
+    scaled = (diff / want.abs().clamp(min=1.0)).max().item()
+    cos = torch.nn.functional.cosine_similarity(got.double(), want.double(), dim=0).item()
+    return {"fixture": "dit_block_nvfp4_gelu.pt", "max_abs": diff.max().item(), "scaled_max_abs": scaled,
+            "cosine": cos, "ok": bool(scaled <= 2e-2 and cos >= 0.9995)}
+
+
+def _phase_table(spans: list, steps: int) -> tuple[list[str], list[float]]:
+    """Per-phase device milliseconds per step, in a fixed phase order."""
+    order = ["norm", "quant", "gemm", "gemm_seq2head", "amax_allreduce", "phase_barrier", "exchange", "rope",
+             "attention"]
+    tot = {n: 0.0 for n in order}
+    for name, ms, _f, _t in spans:
+        tot[name] = tot.get(name, 0.0) + ms
+    names = order + sorted(n for n in tot if n not in order)
+    return names, [tot[n] / steps for n in names]
 
 
 def run_gpu(args) -> None:
@@ -216,7 +357,8 @@ def run_gpu(args) -> None:
 
     from minixmax_h3_b200 import _lib
     from minixmax_h3_b200 import dist as hdist
-    from minixmax_h3_b200.block import ATTN_TIMER, DiTStep, RopeSpec
+    from minixmax_h3_b200.block import DiTStep, RopeSpec
+    from minixmax_h3_b200.timing import TIMER
 
     st = hdist.init(timeout_s=600.0)
     ws, rank = st.world_size, st.rank
@@ -225,9 +367,10 @@ def run_gpu(args) -> None:
     dev = torch.device("cuda", st.local_rank)
     torch.cuda.set_device(dev)
     _lib.lib()
+    _lib.device_status(clear=True)
 
     step = DiTStep(hidden=HIDDEN, heads=HEADS, ffn=FFN, depth=DEPTH, text_dim=TEXT_DIM, fmt="nvfp4",
-                   mlp_act="gelu", device=dev)
+                   mlp_act="gelu", device=dev, seq_parallel="p2p")
     step.init_random(seed=0)  # identical weights on every rank
     rope = RopeSpec.build(positions(), device=dev)
     s_local = S_TOTAL // ws
@@ -258,7 +401,7 @@ def run_gpu(args) -> None:
         torch.cuda.synchronize()
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
         launches0 = _lib.LAUNCHES[0]
-        ATTN_TIMER.enabled = True
+        TIMER.enabled = True
         with ClockSampler(dev.index) as clocks:
             for i in range(args.steps):
                 e = ev[i]
@@ -274,8 +417,8 @@ def run_gpu(args) -> None:
             torch.cuda.synchronize()
             barrier()
             torch.cuda.synchronize()
-        ATTN_TIMER.enabled = False
-        attn = ATTN_TIMER.drain()
+        TIMER.enabled = False
+        spans = TIMER.drain()
         launches = _lib.LAUNCHES[0] - launches0
     step_ms = [e[1].elapsed_time(e[2]) for e in ev]
     compute_ms = sum(step_ms) / args.steps
@@ -284,21 +427,46 @@ def run_gpu(args) -> None:
     if ws > 1:
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
     compute_ms, e2e_ms = t.tolist()
+    # per-phase device time of every rank (same phase order on all ranks)
+    names, mine = _phase_table(spans, args.steps)
+    by_rank = [mine]
+    if ws > 1:
+        vec = torch.tensor(mine, dtype=torch.float64, device=dev)
+        allv = [torch.empty_like(vec) for _ in range(ws)]
+        tdist.all_gather(allv, vec)
+        by_rank = [v.tolist() for v in allv]
+    attn = [(ms, f) for n, ms, f, _ in spans if n == "attention"]
     attn_ms = statistics.mean(a for a, _ in attn)
     attn_flops = attn[0][1]
+    gemms: dict = {}
+    for n, ms, f, tag in spans:
+        if n in ("gemm", "gemm_seq2head"):
+            g = gemms.setdefault((n,) + tuple(tag), [0.0, 0, f])
+            g[0] += ms
+            g[1] += 1
+    top = max(gemms.items(), key=lambda kv: kv[1][0])
+    (g_name, g_fmt, g_m, g_n, g_k), (g_ms, g_count, g_flops) = top
     pk = peaks()
     achieved = attn_flops / (attn_ms * 1e-3) / 1e12
     clock = clocks.summary()
+    # bit-exact sharded-vs-single-GPU and golden checks, on every rank
+    parity = parity_check(ws, rank, dev)
+    torch.cuda.synchronize()
+    status = list(_lib.device_status(clear=False))
+    stat_t = torch.tensor(status, dtype=torch.int64, device=dev)
+    if ws > 1:
+        everyone = [torch.empty_like(stat_t) for _ in range(ws)]
+        tdist.all_gather(everyone, stat_t)
+        statuses = [v.tolist() for v in everyone]
+    else:
+        statuses = [status]
     if rank == 0:
-        # DRAM bytes of one full-size attention launch (S = 498,272, 24 heads),
-        # from the 1-pass ncu capture in profiles/attention_kernel_S131072_H3.md;
-        # a rank's launch covers HEADS/ws heads of the same sequence.
-        traffic = ATTN_DRAM_BYTES_24_HEADS * (HEADS // ws) / HEADS
+        traffic = None if ATTN_DRAM_BYTES_PER_HEAD is None else ATTN_DRAM_BYTES_PER_HEAD * (HEADS // ws)
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
             torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
-            cpu_reference_sample(REF_Q_ROWS, REF_TOKENS)  # warm (weight decode, allocator)
-            rs = [cpu_reference_sample(4 * REF_Q_ROWS, 4 * REF_TOKENS) for _ in range(3)]
+            cpu_reference_sample(WARM_Q_ROWS, WARM_TOKENS)  # warm (weight decode, allocator)
+            rs = [cpu_reference_sample(REF_Q_ROWS, REF_TOKENS) for _ in range(3)]
             cpu = {"value": statistics.mean(r["value"] for r in rs), "unit": UNIT, "cores": torch.get_num_threads(),
                    "kind": "port", "sample": "mean of 3 x " + rs[0]["sample"]}
         line = {
@@ -306,14 +474,23 @@ def run_gpu(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": compute_ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4 (e2m1/e4m3) GEMMs + bf16 attention",
             "data": "synthetic (random-init weights, N(0,1) bf16 inputs)",
-            "config": {"workload": WORKLOAD, "seq_len": S_TOTAL, "blocks": DEPTH, "hidden": HIDDEN, "heads": HEADS,
-                       "mlp": FFN, "parallelism": f"ulysses{ws}", "l2": "inputs larger than L2 (>= 3 GB tensors)"},
+            "config": _config(ws),
             "e2e": {"value": S_TOTAL * DEPTH / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": {"kernel": "attention_kernel (tcgen05 flash attention)", "bound": "tensor",
                          "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s", "frac": achieved / pk["bf16"],
                          "peak_kind": f"bf16 sustained ({pk['source']})", "traffic": traffic,
+                         "traffic_kind": "ncu DRAM bytes of a 1-head launch at this S, times heads per rank",
                          "launch_ms": attn_ms, "flops_per_launch": attn_flops},
+            "gemm_roofline": {"kernel": f"gemm_kernel NVFP4 ({g_name}: M={g_m} N={g_n} K={g_k})", "format": g_fmt,
+                              "bound": "tensor", "achieved": g_flops / (g_ms / g_count * 1e-3) / 1e12,
+                              "peak": 9000.0, "unit": "TFLOP/s",
+                              "frac": g_flops / (g_ms / g_count * 1e-3) / 1e12 / 9000.0,
+                              "peak_kind": "B200 dense FP4 spec (no measured FP4 peak on this pool)",
+                              "launch_ms": g_ms / g_count, "launches": g_count},
+            "phases": {"names": names, "ms_per_step_by_rank": [[round(v, 2) for v in r] for r in by_rank]},
+            "parity": parity,
+            "device_status": statuses,
             "cpu_baseline": cpu,
             "clocks": clock,
             "gpu_launches": launches,
@@ -323,6 +500,11 @@ def run_gpu(args) -> None:
     if ws > 1:
         barrier()
     hdist.destroy()
+    bad = [s for s in statuses if s[0] != 0]
+    failed = rank == 0 and (bad or (parity.get("sharded_vs_one_gpu") or {}).get("exact") is False
+                            or not parity["golden"]["ok"])
+    if failed:
+        raise SystemExit(f"bench: device status {statuses} / parity {parity}")
 
 
 def main() -> None:

@@ -308,6 +308,21 @@ H3B_API int h3b_attention_fwd_head2seq(const void* q, const void* k, const void*
                                        int64_t kv_seq_stride, int64_t kv_head_stride, float scale,
                                        h3b_stream_t stream);
 
+/*
+ * Self-test of the bounded device waits; no counterpart in the reference,
+ * whose distributed waits are host-side timeouts (runtime/dist.py:43,99-116).
+ * Launches the NVFP4 GEMM of h3b_gemm_nvfp4_bf16 on the given operands (one
+ * output tile: m <= 128, n <= 192) with its producer issuing no loads, so no
+ * copy is ever in flight and the MMA thread's wait for the first K slab can
+ * never complete.  The wait runs out after its budget (2 s), records
+ * H3B_ERR_DEVICE_TIMEOUT with site 3 in the device status word, and every
+ * warp unwinds; the kernel frees its TMEM and returns without writing y.
+ * Returns the launch status; read the outcome with h3b_device_status().
+ */
+H3B_API int h3b_selftest_wait_timeout(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                      const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs, void* y,
+                                      int64_t m, int64_t n, int64_t k, h3b_stream_t stream);
+
 /* Merge of an attention result over one key chunk into a running result
  * over earlier chunks through the rows' log-sum-exps, in fp32 — the ring
  * sequence-parallel step of ops/fa_h3.py:141-156 (_merge_lse), used by

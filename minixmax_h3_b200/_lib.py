@@ -46,6 +46,7 @@ SIGNATURES: dict[str, list] = {
                                       c_ptr, c_ptr, c_ptr],
     "h3b_rmsnorm_modulate_quant_nvfp4_noalloc": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
                                                  c_f32, c_ptr, c_ptr, c_ptr, c_int, c_ptr],
+    "h3b_selftest_wait_timeout": [c_ptr] * 7 + [c_i64] * 3 + [c_ptr],
     "h3b_attention_merge_lse": [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_int, c_ptr, c_ptr, c_ptr],
 }
 

@@ -30,6 +30,7 @@ from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantizedRows, QuantLinear, RMSNorm
 from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
+from .timing import TIMER
 from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, check_scheme, clip_mod_segments,
                       peer_buffer, phase_barrier, ring_attention, split_range)
 
@@ -72,7 +73,8 @@ def global_amax_(amax: Optional[torch.Tensor], ql: QuantLinear) -> Optional[torc
     if amax is not None and ql.quant_format == "nvfp4" and is_distributed():
         import torch.distributed as tdist
 
-        tdist.all_reduce(amax, op=tdist.ReduceOp.MAX, group=state().group)
+        with TIMER.span("amax_allreduce"):
+            tdist.all_reduce(amax, op=tdist.ReduceOp.MAX, group=state().group)
     return amax
 
 
@@ -104,35 +106,6 @@ class AdalnProj(nn.Module):
         x = self.linear(F.silu(t_emb) if self.apply_silu else t_emb)
         x = x.to(torch.bfloat16).reshape(x.shape[0] * self.modalities, self.expand * self.hidden)
         return x.chunk(self.expand, dim=-1)
-
-
-class KernelTimer:
-    """Optional CUDA-event bracketing of the attention launches (used by the
-    benchmark to time the dominant kernel live inside a step)."""
-
-    def __init__(self):
-        self.pairs: list[tuple[torch.cuda.Event, torch.cuda.Event, float]] = []
-        self.enabled = False
-
-    def record(self, fn, flops: float):
-        if not self.enabled:
-            return fn()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        out = fn()
-        b.record()
-        self.pairs.append((a, b, flops))
-        return out
-
-    def drain(self) -> list[tuple[float, float]]:
-        """[(milliseconds, flops)] of the recorded launches (synchronises)."""
-        torch.cuda.synchronize()
-        out = [(a.elapsed_time(b), f) for a, b, f in self.pairs]
-        self.pairs.clear()
-        return out
-
-
-ATTN_TIMER = KernelTimer()
 
 
 class Attention(nn.Module):
@@ -170,47 +143,52 @@ class Attention(nn.Module):
         ring = sp and self.seq_parallel == "ring"
         qkv = self.qkv_proj.forward_fused(h, amax=global_amax_(amax_h, self.qkv_proj))  # [S_l, 3*H*D]
         q3 = qkv.view(s_local, 3, self.heads, self.head_dim)
-        if rope_freqs is not None:
-            s0 = split_range(rope_freqs.pos.shape[0])[0] if sp else 0
-            ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
-                                rope_freqs.pos, s0, rope_freqs.inv_freq, rope_freqs.n_t, rope_freqs.n_h)
-        else:
-            # q/k RMSNorm only (RoPE-free blocks): fold into the rope kernel
-            # with zero frequencies (cos 1, sin 0).
-            zeros = torch.zeros(64, dtype=torch.float32, device=h.device)
-            pos0 = torch.zeros(s_local, 3, dtype=torch.float32, device=h.device)
-            ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
-                                pos0, 0, zeros, 64, 0)
+        with TIMER.span("rope"):
+            if rope_freqs is not None:
+                s0 = split_range(rope_freqs.pos.shape[0])[0] if sp else 0
+                ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
+                                    rope_freqs.pos, s0, rope_freqs.inv_freq, rope_freqs.n_t, rope_freqs.n_h)
+            else:
+                # q/k RMSNorm only (RoPE-free blocks): fold into the rope kernel
+                # with zero frequencies (cos 1, sin 0).
+                zeros = torch.zeros(64, dtype=torch.float32, device=h.device)
+                pos0 = torch.zeros(s_local, 3, dtype=torch.float32, device=h.device)
+                ops.qk_rmsnorm_rope(q3[:, 0], q3[:, 1], self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
+                                    pos0, 0, zeros, 64, 0)
         amax_o = torch.zeros(1, dtype=torch.float32, device=h.device)
         if ring:
             # ring SP (ops/fa_h3.py:159-218): local queries, K/V chunks passed
             # around the ring, chunk results merged through their LSEs
             flops = 4.0 * s_local * s_local * state().world_size * self.head_dim * self.heads
-            o = ATTN_TIMER.record(lambda: ring_attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5,
-                                                         amax_out=amax_o), flops)
+            with TIMER.span("attention", flops):
+                o = ring_attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5, amax_out=amax_o)
             o = o.view(s_local, self.heads * self.head_dim)
             global_amax_(amax_o, self.out_proj)
         elif gather_kv:
             # the reference's production SP (model/dit.py:200-248): local
             # queries over the gathered keys/values of all ranks, all heads
-            k, v = all_gather_kv(q3[:, 1], q3[:, 2])
+            with TIMER.span("exchange"):
+                k, v = all_gather_kv(q3[:, 1], q3[:, 2])
             flops = 4.0 * s_local * k.shape[0] * self.head_dim * self.heads
-            o = ATTN_TIMER.record(lambda: ops.attention(q3[:, 0], k, v, scale=self.head_dim ** -0.5,
-                                                        amax_out=amax_o), flops)
+            with TIMER.span("attention", flops):
+                o = ops.attention(q3[:, 0], k, v, scale=self.head_dim ** -0.5, amax_out=amax_o)
             o = o.view(s_local, self.heads * self.head_dim)
             global_amax_(amax_o, self.out_proj)
         elif sp:
-            q, k, v = all_to_all_qkv(qkv, self.heads, self.head_dim)
+            with TIMER.span("exchange"):
+                q, k, v = all_to_all_qkv(qkv, self.heads, self.head_dim)
             flops = 4.0 * q.shape[0] * k.shape[0] * self.head_dim * q.shape[1]
-            o = ATTN_TIMER.record(lambda: ops.attention(q, k, v, scale=self.head_dim ** -0.5), flops)
-            o = all_to_all_heads(o, gather_seq=False).reshape(s_local, self.heads * self.head_dim)
-            o = o.contiguous()
+            with TIMER.span("attention", flops):
+                o = ops.attention(q, k, v, scale=self.head_dim ** -0.5)
+            with TIMER.span("exchange"):
+                o = all_to_all_heads(o, gather_seq=False).reshape(s_local, self.heads * self.head_dim)
+                o = o.contiguous()
             ops.amax(o, out=amax_o)
             global_amax_(amax_o, self.out_proj)
         else:
             flops = 4.0 * s_local * s_local * self.head_dim * self.heads
-            o = ATTN_TIMER.record(lambda: ops.attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5,
-                                                        amax_out=amax_o), flops)
+            with TIMER.span("attention", flops):
+                o = ops.attention(q3[:, 0], q3[:, 1], q3[:, 2], scale=self.head_dim ** -0.5, amax_out=amax_o)
             o = o.view(s_local, self.heads * self.head_dim)
         if resid is not None:
             return self.out_proj.forward_fused(o, amax=amax_o, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
@@ -233,21 +211,25 @@ class Attention(nn.Module):
         recv = peer_buffer("ulysses_qkv", (s_full, 3, hl, self.head_dim), torch.bfloat16, h.device)
         obuf = peer_buffer("ulysses_o", (s_local, self.heads, self.head_dim), torch.bfloat16, h.device)
         self.qkv_proj.forward_seq2head(h, recv.ptrs, rank, self.heads, amax=global_amax_(amax_h, self.qkv_proj))
-        phase_barrier(h.device)
+        with TIMER.span("phase_barrier"):
+            phase_barrier(h.device)
         q, k, v = recv.local[:, 0], recv.local[:, 1], recv.local[:, 2]
-        if rope_freqs is not None:
-            ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, rope_freqs.pos, 0,
-                                rope_freqs.inv_freq, rope_freqs.n_t, rope_freqs.n_h)
-        else:
-            zeros = torch.zeros(64, dtype=torch.float32, device=h.device)
-            pos0 = torch.zeros(s_full, 3, dtype=torch.float32, device=h.device)
-            ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, pos0, 0, zeros, 64, 0)
+        with TIMER.span("rope"):
+            if rope_freqs is not None:
+                ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, rope_freqs.pos,
+                                    0, rope_freqs.inv_freq, rope_freqs.n_t, rope_freqs.n_h)
+            else:
+                zeros = torch.zeros(64, dtype=torch.float32, device=h.device)
+                pos0 = torch.zeros(s_full, 3, dtype=torch.float32, device=h.device)
+                ops.qk_rmsnorm_rope(q, k, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps, pos0, 0, zeros,
+                                    64, 0)
         amax_o = torch.zeros(1, dtype=torch.float32, device=h.device)
         flops = 4.0 * s_full * s_full * self.head_dim * hl
-        ATTN_TIMER.record(lambda: ops.attention_head2seq(q, k, v, obuf.ptrs, s_local=s_local, head0=rank * hl,
-                                                         total_heads=self.heads, scale=self.head_dim ** -0.5,
-                                                         amax_out=amax_o), flops)
-        phase_barrier(h.device, amax_o)  # orders the O stores; amax_o is now the global max
+        with TIMER.span("attention", flops):
+            ops.attention_head2seq(q, k, v, obuf.ptrs, s_local=s_local, head0=rank * hl, total_heads=self.heads,
+                                   scale=self.head_dim ** -0.5, amax_out=amax_o)
+        with TIMER.span("phase_barrier"):
+            phase_barrier(h.device, amax_o)  # orders the O stores; amax_o is now the global max
         o = obuf.local.view(s_local, self.heads * self.head_dim)
         if resid is not None:
             return self.out_proj.forward_fused(o, amax=amax_o, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
@@ -330,14 +312,16 @@ class DiTBlock(nn.Module):
                 # norm + modulate + (ConvRot) + row quantisation in one kernel
                 # (a pre_quant_scale applies between the two: the layer does it)
                 group = ql.group_size if ql.convrot else 0
-                q, xs = ops.rmsnorm_modulate_quant_i8(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
-                                                      convrot_group=group,
-                                                      q_out=h.q if isinstance(h, QuantizedRows) else None,
-                                                      scale_out=h.scale if isinstance(h, QuantizedRows) else None)
+                with TIMER.span("norm"):
+                    q, xs = ops.rmsnorm_modulate_quant_i8(
+                        x, norm.weight, shift, scale, norm.eps, row_sel=sel, convrot_group=group,
+                        q_out=h.q if isinstance(h, QuantizedRows) else None,
+                        scale_out=h.scale if isinstance(h, QuantizedRows) else None)
                 h = QuantizedRows(q, xs, group)
             else:
-                h = ops.rmsnorm_modulate(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
-                                         amax_out=amax[i:i + 1], out=h if isinstance(h, torch.Tensor) else None)
+                with TIMER.span("norm"):
+                    h = ops.rmsnorm_modulate(x, norm.weight, shift, scale, norm.eps, row_sel=sel,
+                                             amax_out=amax[i:i + 1], out=h if isinstance(h, torch.Tensor) else None)
             if i == 0:
                 sub(h, rope_freqs, amax_h=amax[0:1], resid=x, gate=gate, row_sel=sel)
             else:

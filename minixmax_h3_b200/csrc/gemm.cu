@@ -95,6 +95,7 @@ struct GemmArgs {
   int out_mode;
   int heads_per_rank;  // OUT_SEQ2HEAD: H / world_size
   int hd;              // OUT_SEQ2HEAD: H * 128 (columns per q|k|v part)
+  int no_loads;        // wait self-test: the producer issues nothing (h3b_selftest_wait_timeout)
 };
 
 // PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per
@@ -235,7 +236,9 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // (no_loads: nothing is issued, so no copy is ever in flight and the
+    // consumers' first waits can only run out)
+    if (lane == 0 && !args.no_loads) {
       int it = 0;
       bool ok = true;
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
@@ -853,4 +856,39 @@ extern "C" int h3b_gemm_nvfp4_seq2head(const uint8_t* a_codes, const uint8_t* a_
   a.n = static_cast<int>(n);
   a.k = static_cast<int>(k);
   return launch_gemm<KIND_NVF4>(a_codes, w_codes, k / 2, k / 2, a, reinterpret_cast<cudaStream_t>(stream), &maps);
+}
+
+// Self-test of the bounded waits (no reference counterpart).  The NVFP4 GEMM
+// kernel is launched on the caller's operands with its producer issuing no
+// loads: no TMA or bulk copy is ever started, so the MMA thread's wait for
+// the first slab can never complete.  After the 2 s budget it records
+// H3B_ERR_DEVICE_TIMEOUT (site 3, the MMA thread's full-barrier wait), raises
+// the CTA's abort flag, and every other warp leaves its own wait; the kernel
+// frees its TMEM and returns.  Nothing is written to y.
+extern "C" int h3b_selftest_wait_timeout(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
+                                         const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs, void* y,
+                                         int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {
+  if (a_codes == nullptr || a_sf == nullptr || a_gs == nullptr || w_codes == nullptr || w_sf == nullptr ||
+      w_gs == nullptr || y == nullptr)
+    return H3B_ERR_ARG;
+  int rc = check_common(m, n, k, 256);
+  if (rc != H3B_OK) return rc;
+  if (m == 0 || m > BM || n > 192) return H3B_ERR_SHAPE;  // one output tile, one CTA
+  if (!h3b::aligned16(a_codes) || !h3b::aligned16(w_codes) || !h3b::aligned16(y) || !h3b::aligned16(a_sf) ||
+      !h3b::aligned16(w_sf))
+    return H3B_ERR_ALIGN;
+  GemmArgs a{};
+  a.a_gs = a_gs;
+  a.w_gs = w_gs;
+  a.a_sf = a_sf;
+  a.w_sf = w_sf;
+  a.y = y;
+  a.ldy = n;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.epilogue = H3B_EPI_STORE;
+  a.out_mode = OUT_BF16;
+  a.no_loads = 1;
+  return launch_gemm<KIND_NVF4>(a_codes, w_codes, k / 2, k / 2, a, reinterpret_cast<cudaStream_t>(stream));
 }

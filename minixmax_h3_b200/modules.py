@@ -19,6 +19,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .ops import EPI_STORE, NVFP4Tensor
+from .timing import TIMER
 
 
 class RMSNorm(nn.Module):
@@ -245,17 +246,26 @@ class QuantLinear(nn.Module):
              row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
              out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.quant_format == "int8_tensorwise":
-            q, xs = self._quant_i8_input(x)
-            return ops.gemm_i8(q, xs, self.weight_i8, self.weight_scale, self._bias(x), epilogue=epilogue,
-                               resid=resid, gate=gate, row_sel=row_sel, amax_out=amax_out, out=out)
+            with TIMER.span("quant"):
+                q, xs = self._quant_i8_input(x)
+            with TIMER.span("gemm", *self._gemm_cost(q.shape[0])):
+                return ops.gemm_i8(q, xs, self.weight_i8, self.weight_scale, self._bias(x), epilogue=epilogue,
+                                   resid=resid, gate=gate, row_sel=row_sel, amax_out=amax_out, out=out)
         if self.quant_format == "nvfp4":
             self.prepare_cube()
             if isinstance(x, QuantizedRows):
                 raise TypeError("an NVFP4 layer needs the bf16 input, not INT8 QuantizedRows")
-            a = ops.quant_nvfp4(x, amax_t=amax)
-            return ops.gemm_nvfp4(a, self._w_nvfp4, self._bias(x), epilogue=epilogue, resid=resid, gate=gate,
-                                  row_sel=row_sel, amax_out=amax_out, out=out)
+            with TIMER.span("quant"):
+                a = ops.quant_nvfp4(x, amax_t=amax)
+            with TIMER.span("gemm", *self._gemm_cost(a.rows)):
+                return ops.gemm_nvfp4(a, self._w_nvfp4, self._bias(x), epilogue=epilogue, resid=resid, gate=gate,
+                                      row_sel=row_sel, amax_out=amax_out, out=out)
         raise RuntimeError("QuantLinear has no quantised weights (call set_quant first)")
+
+    def _gemm_cost(self, m: int) -> tuple[float, tuple]:
+        """(flops, (format, m, n, k)) of one GEMM launch over m rows."""
+        return 2.0 * m * self.out_features * self.in_features, (self.quant_format, m, self.out_features,
+                                                                 self.in_features)
 
     def forward_seq2head(self, x: torch.Tensor, recv_ptrs, rank: int, heads: int, *,
                          amax: Optional[torch.Tensor] = None) -> None:
@@ -264,15 +274,20 @@ class QuantLinear(nn.Module):
         seq->head Ulysses exchange in one kernel."""
         x, amax = self._pre_scale(x, amax)
         if self.quant_format == "int8_tensorwise":
-            q, xs = self._quant_i8_input(x)
-            ops.gemm_i8_seq2head(q, xs, self.weight_i8, self.weight_scale, self._bias(x), recv_ptrs, rank, heads)
+            with TIMER.span("quant"):
+                q, xs = self._quant_i8_input(x)
+            with TIMER.span("gemm_seq2head", *self._gemm_cost(q.shape[0])):
+                ops.gemm_i8_seq2head(q, xs, self.weight_i8, self.weight_scale, self._bias(x), recv_ptrs, rank,
+                                     heads)
             return
         if self.quant_format == "nvfp4":
             self.prepare_cube()
             if isinstance(x, QuantizedRows):
                 raise TypeError("an NVFP4 layer needs the bf16 input, not INT8 QuantizedRows")
-            a = ops.quant_nvfp4(x, amax_t=amax)
-            ops.gemm_nvfp4_seq2head(a, self._w_nvfp4, self._bias(x), recv_ptrs, rank, heads)
+            with TIMER.span("quant"):
+                a = ops.quant_nvfp4(x, amax_t=amax)
+            with TIMER.span("gemm_seq2head", *self._gemm_cost(a.rows)):
+                ops.gemm_nvfp4_seq2head(a, self._w_nvfp4, self._bias(x), recv_ptrs, rank, heads)
             return
         raise RuntimeError("QuantLinear has no quantised weights (call set_quant first)")
 

@@ -192,7 +192,7 @@ def from_blocked(flat: np.ndarray, rows: int, ncols: int) -> np.ndarray:
     return flat[blocked_offset(r, c, ncols)]
 
 
-def nvfp4_quantize(x: torch.Tensor, hi_first: bool = True) -> dict:
+def nvfp4_quantize(x: torch.Tensor, hi_first: bool = True, amax: Optional[float] = None) -> dict:
     """NVFP4 quantiser restated from the published recipe (e2m1 values, one
     e4m3 scale per 16 elements, fp32 global scale):
 
@@ -202,12 +202,17 @@ def nvfp4_quantize(x: torch.Tensor, hi_first: bool = True) -> dict:
 
     Codes are packed two per byte (hi_first: even element in the high nibble,
     the order ops/nvfp4.py:113-121 decodes); scales in the blocked layout.
+    `amax` overrides max|x| for rows sampled from a larger tensor, whose
+    global scale comes from the whole tensor.
     """
     xf = x.float().numpy().astype(np.float32)
     m, k = xf.shape
     if k % 16:
         raise ValueError("k must be a multiple of 16")
-    amax = np.float32(np.abs(xf).max()) if xf.size else np.float32(0)
+    if amax is not None:
+        amax = np.float32(amax)
+    else:
+        amax = np.float32(np.abs(xf).max()) if xf.size else np.float32(0)
     gs = np.float32(amax / np.float32(2688.0)) if amax > 0 else np.float32(1.0)
     six_gs = np.float32(np.float32(6.0) * gs)
     blocks = xf.reshape(m, k // 16, 16)

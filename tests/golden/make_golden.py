@@ -24,9 +24,12 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
+sys.path.insert(0, str(HERE.parent))
 
 from oracle import h3_oracle as O  # noqa: E402
 from oracle import reference  # noqa: E402
+
+from golden.fixture_params import block_fixture_params  # noqa: E402,F401  (re-exported)
 
 
 def outlier_activations(g: torch.Generator, m: int, k: int) -> torch.Tensor:
@@ -96,34 +99,7 @@ def make_attention(R) -> dict:
     return {"q": q, "k": k, "v": v, "out": out}
 
 
-def block_params(g: torch.Generator, hidden: int, heads: int, ffn_out: int, ffn_in: int, t_dim: int) -> dict:
-    """Seeded block weights (bf16).  The fixtures store only the seed; tests
-    call this again with the same generator state to rebuild them."""
-    inner = heads * 128
-    p = {
-        "qkv_w": torch.randn(3 * inner, hidden, generator=g) * 0.02,
-        "out_w": torch.randn(hidden, inner, generator=g) * 0.02,
-        "fc1_w": torch.randn(ffn_out, hidden, generator=g) * 0.02,
-        "fc2_w": torch.randn(hidden, ffn_in, generator=g) * 0.02,
-        "adaln_w": torch.randn(6 * hidden * 3, t_dim, generator=g) * 0.02,
-        "adaln_b": torch.randn(6 * hidden * 3, generator=g) * 0.02,
-        "norm1_w": 1.0 + 0.1 * torch.randn(hidden, generator=g),
-        "norm2_w": 1.0 + 0.1 * torch.randn(hidden, generator=g),
-        "q_norm_w": 1.0 + 0.1 * torch.randn(128, generator=g),
-        "k_norm_w": 1.0 + 0.1 * torch.randn(128, generator=g),
-    }
-    return {k: v.to(torch.bfloat16) for k, v in p.items()}
-
-
 BLOCK_CFG = {"hidden": 256, "heads": 2, "t_dim": 32, "eps": 1e-6, "qk_eps": 1e-6, "grid": (1, 8, 16)}
-
-
-def block_fixture_params(fix: dict) -> dict:
-    """Rebuilds the weights of a block fixture from its seed."""
-    g = torch.Generator().manual_seed(fix["seed"])
-    hidden, ffn = fix["hidden"], 4 * fix["hidden"]
-    ffn_out = ffn if fix["mlp_act"] == "gelu" else 2 * ffn
-    return block_params(g, hidden, fix["heads"], ffn_out, ffn, fix["t_dim"])
 
 
 def make_block(R, fmt: str, mlp_act: str, seed: int = 4) -> dict:
