@@ -314,9 +314,12 @@ H3B_API int h3b_attention_fwd_head2seq(const void* q, const void* k, const void*
  * Launches the NVFP4 GEMM of h3b_gemm_nvfp4_bf16 on the given operands (one
  * output tile: m <= 128, n <= 192) with its producer issuing no loads, so no
  * copy is ever in flight and the MMA thread's wait for the first K slab can
- * never complete.  The wait runs out after its budget (2 s), records
- * H3B_ERR_DEVICE_TIMEOUT with site 3 in the device status word, and every
- * warp unwinds; the kernel frees its TMEM and returns without writing y.
+ * never complete, nor can the waits of the other warps behind it.  The
+ * waits run out after their budget (2 s); the first records
+ * H3B_ERR_DEVICE_TIMEOUT and its site in the device status word (3: the MMA
+ * thread's slab wait, 4: an epilogue warp's accumulator wait, 7: a scale
+ * writer's wait), and every warp unwinds; the kernel frees its TMEM and
+ * returns without writing y.
  * Returns the launch status; read the outcome with h3b_device_status().
  */
 H3B_API int h3b_selftest_wait_timeout(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,

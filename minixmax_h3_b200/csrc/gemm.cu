@@ -861,10 +861,11 @@ extern "C" int h3b_gemm_nvfp4_seq2head(const uint8_t* a_codes, const uint8_t* a_
 // Self-test of the bounded waits (no reference counterpart).  The NVFP4 GEMM
 // kernel is launched on the caller's operands with its producer issuing no
 // loads: no TMA or bulk copy is ever started, so the MMA thread's wait for
-// the first slab can never complete.  After the 2 s budget it records
-// H3B_ERR_DEVICE_TIMEOUT (site 3, the MMA thread's full-barrier wait), raises
-// the CTA's abort flag, and every other warp leaves its own wait; the kernel
-// frees its TMEM and returns.  Nothing is written to y.
+// the first slab can never complete, nor can the scale writers' and the
+// epilogue's waits behind it.  After the 2 s budget the first wait to run out
+// records H3B_ERR_DEVICE_TIMEOUT and its site (3, 4 or 7), raises the CTA's
+// abort flag, and every other warp leaves its own wait; the kernel frees its
+// TMEM and returns.  Nothing is written to y.
 extern "C" int h3b_selftest_wait_timeout(const uint8_t* a_codes, const uint8_t* a_sf, const float* a_gs,
                                          const uint8_t* w_codes, const uint8_t* w_sf, const float* w_gs, void* y,
                                          int64_t m, int64_t n, int64_t k, h3b_stream_t stream) {

@@ -3,10 +3,12 @@
 h3b_selftest_wait_timeout launches the NVFP4 GEMM with its producer issuing no
 loads: no copy is ever in flight, and the MMA thread's wait for the first K
 slab is a wait on a barrier that nothing will complete.  The wait must run
-out after its budget (2 s), the device status must name the timeout and the
-site (3: the MMA thread's full-barrier wait), the kernel must return without
-writing its output, and the next ordinary launch on the same context must
-give the same bits as before.  No trap, no fault, no unbounded wait.  (The
+out after its budget (2 s), and the device status must name the timeout and
+the site of the first wait to run out (3: the MMA thread's wait for the slab;
+4: an epilogue warp's wait for the accumulator; 7: a scale writer's wait for
+the slab's scales — all start together on barriers nothing completes).  The
+kernel must return without writing its output, and the next ordinary launch
+on the same context must give the same bits as before.  No trap, no fault, no unbounded wait.  (The
 reference's counterparts are host-side timeouts: runtime/dist.py:43,99-116.)"""
 from __future__ import annotations
 
@@ -18,7 +20,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 H3B_ERR_DEVICE_TIMEOUT = 6
-SITE_MMA_FULL_WAIT = 3
+CONSUMER_SITES = {3, 4, 7}  # MMA slab wait, epilogue accumulator wait, scale-writer wait
 
 
 def test_bounded_wait_runs_out_and_the_context_stays_usable(cuda):
@@ -38,7 +40,7 @@ def test_bounded_wait_runs_out_and_the_context_stays_usable(cuda):
               torch.cuda.current_stream(cuda).cuda_stream)
     code, site, _info, block = _lib.device_status(clear=True)  # synchronises
     elapsed = time.monotonic() - t0
-    assert (code, site, block) == (H3B_ERR_DEVICE_TIMEOUT, SITE_MMA_FULL_WAIT, 0)
+    assert code == H3B_ERR_DEVICE_TIMEOUT and site in CONSUMER_SITES and block == 0, (code, site, block)
     assert 1.5 <= elapsed <= 20.0, elapsed  # the 2 s budget, not a hang
     assert torch.isnan(y.float()).all()  # the unwound kernel wrote nothing
 

@@ -81,14 +81,25 @@ def test_noalloc_wide_row_stride_and_no_row_sel(cuda):
 
 
 def test_noalloc_rejects_sizes_beyond_its_array(cuda):
-    from minixmax_h3_b200._lib import H3bError
+    """Rows beyond the 16 MiB array: H3B_ERR_SHAPE before anything is
+    queued (the output pointers are valid but far too small; the entry point
+    never reaches them).  A null output is refused as such, also before any
+    work."""
+    from minixmax_h3_b200._lib import H3bError, call
 
     x, w, shift, scale, sel = _inputs(2, 64, 1024, cuda)
+    codes = torch.empty(64, 512, dtype=torch.uint8, device=cuda)
+    sf = torch.empty(128 * 64, dtype=torch.uint8, device=cuda)
+    gs = torch.empty(1, dtype=torch.float32, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
     too_many = (16 << 20) // (2 * 1024) + 1  # rows of 1024 bf16 beyond the 16 MiB array
     with pytest.raises(H3bError) as e:
-        from minixmax_h3_b200._lib import call
-
         call("h3b_rmsnorm_modulate_quant_nvfp4_noalloc", x.data_ptr(), too_many, 1024, 1024, w.data_ptr(),
-             shift.data_ptr(), scale.data_ptr(), shift.stride(0), sel.data_ptr(), 1e-6, 0, 0, 0, 1,
-             torch.cuda.current_stream(cuda).cuda_stream)
+             shift.data_ptr(), scale.data_ptr(), shift.stride(0), sel.data_ptr(), 1e-6, codes.data_ptr(),
+             sf.data_ptr(), gs.data_ptr(), 1, stream)
     assert e.value.code == 1  # H3B_ERR_SHAPE
+    with pytest.raises(H3bError) as e:
+        call("h3b_rmsnorm_modulate_quant_nvfp4_noalloc", x.data_ptr(), 64, 1024, 1024, w.data_ptr(),
+             shift.data_ptr(), scale.data_ptr(), shift.stride(0), sel.data_ptr(), 1e-6, None, sf.data_ptr(),
+             gs.data_ptr(), 1, stream)
+    assert e.value.code == 8  # H3B_ERR_ARG
