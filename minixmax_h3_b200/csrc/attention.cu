@@ -8,7 +8,8 @@
 // over all 128-row K/V tiles of that head:
 //   warps 0-3   softmax for Q0 (thread = query row = TMEM lane)
 //   warps 4-7   softmax for Q1
-//   warp 8      TMA producer: Q0/Q1 once, K and V through 2-deep rings
+//   warp 8      TMA producer: Q0/Q1 once, K through a 2-deep ring, V through
+//               a 3-deep ring (one release wait per K/V tile covers both)
 //   warp 9      TMEM allocator + single-thread MMA issuer
 //   warps 10-11 idle (complete the third warpgroup for setmaxnreg)
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each.  The softmax
@@ -22,6 +23,17 @@
 // columns: the tcgen05.mma stream of one thread executes in order, so the
 // write cannot overtake the read.  The commit after S_i(j) also covers
 // PV_i(j-1), so when a softmax sees S_i(j) ready, O_i is settled.
+// The issuing thread sits on each tile's critical path (softmax -> P.V ->
+// S -> softmax), so it commits three times per K/V tile: S_0(j+1) ready,
+// S_1(j+1) ready, and kv_free(j) right behind S_0(j+1) (it covers every MMA
+// issued before), which releases K_j (both S MMAs read it) and V_{j-1} (both
+// P.V MMAs read it); S_0(j+1) follows PV_0(j) in straight-line code.  The
+// final commit publishes both O tiles.
+// After the first K/V tile a softmax exponentiates half 0 against its
+// running max while it finds the tile's row max on the ALU alongside; only a
+// row whose max outgrew the running max by more than the threshold sends
+// its warp back to reload S from TMEM (P has not been written over it yet)
+// and rescale first.
 // The row max is rescaled lazily: O and the row sum are corrected only when
 // the running max grows by more than 8 (log2 domain), which bounds P by 2^8.
 // Head->sequence scatter (h3b_attention_fwd_head2seq, the Ulysses exchange
@@ -45,7 +57,7 @@ constexpr int D = 128;
 constexpr int BQ = 128;    // rows per Q tile (one softmax warpgroup)
 constexpr int BKV = 128;   // rows per K/V tile
 constexpr int KST = 2;     // K ring depth
-constexpr int VST = 2;     // V ring depth
+constexpr int VST = 3;     // V ring depth: V_j's slot is free at kv_free(j-2), like K_j's
 constexpr int Q_TILE_BYTES = BQ * D * 2;        // 32 KB: two 16 KB boxes (d 0-63, 64-127)
 constexpr int Q_HALF_BYTES = Q_TILE_BYTES / 2;
 constexpr int KV_TILE_BYTES = BKV * D * 2;      // 32 KB: two 16 KB boxes
@@ -69,16 +81,16 @@ __host__ __device__ constexpr uint32_t o_col(int i) { return static_cast<uint32_
 struct __align__(8) Bars {
   uint64_t q_full;
   uint64_t k_full[KST];
-  uint64_t k_empty[KST];
   uint64_t v_full[VST];
-  uint64_t v_empty[VST];
+  uint64_t kv_free[2];     // [j % 2]: K_j and V_{j-1} no longer read (tcgen05.commit behind S_0(j+1))
   uint64_t s_full[2];      // [tile]: S_i(j) ready (tcgen05.commit)
   uint64_t p_half[2][2];   // [tile][half]: P_i(j) columns 64h..64h+63 written (one arrival per softmax warp)
-  uint64_t pv_done[2];     // [tile]: O_i += P_i(j) V_j complete (tcgen05.commit)
+  uint64_t o_done;         // both O tiles final (one phase; tcgen05.commit after the last P.V)
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
+static_assert(KST == 2 && VST == 3, "the producer's single kv_free wait per tile assumes these ring depths");
 
 constexpr size_t SMEM_BYTES = 1024 + 2 * Q_TILE_BYTES + KST * KV_TILE_BYTES + VST * KV_TILE_BYTES + sizeof(Bars);
 
@@ -164,15 +176,27 @@ constexpr int POLY_PAIRS_PER_8 = 0;
 // bf16 P out in dst[0..31]): packed fp32x2 FMA, 64 independent exponentials
 // (split between MUFU ex2 and the FMA-pipe polynomial), then pack and packed
 // sums.  dst may alias r (dst[e] is written after r[2e], r[2e+1] are read,
-// and e <= 2e).  Returns the partial row sum.
-template <bool MASK>
-H3B_DEV float exp_pack64(uint32_t* r, uint32_t* dst, int valid, float scale_log2, float neg_m) {
+// and e <= 2e).  Returns the partial row sum.  With MAX, the raw max of all
+// 128 columns r[0..127] is found alongside (r[0..63] read before they are
+// overwritten, r[64..127] untouched), so the ALU max work runs under the MUFU
+// work; it is returned in .y.
+template <bool MASK, bool MAX = false>
+H3B_DEV float2 exp_pack64(uint32_t* r, uint32_t* dst, int valid, float scale_log2, float neg_m) {
   const float2 sc = make_float2(scale_log2, scale_log2);
   const float2 nm = make_float2(neg_m, neg_m);
+  float mx[8];
+  if constexpr (MAX) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) mx[c] = -INFINITY;
+  }
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const float sa = (!MASK || 2 * e < valid) ? __uint_as_float(r[2 * e]) : -INFINITY;
     const float sb = (!MASK || 2 * e + 1 < valid) ? __uint_as_float(r[2 * e + 1]) : -INFINITY;
+    if constexpr (MAX) {
+      mx[e & 7] = fmax3(mx[e & 7], sa, sb);
+      mx[e & 7] = fmax3(mx[e & 7], __uint_as_float(r[64 + 2 * e]), __uint_as_float(r[64 + 2 * e + 1]));
+    }
     float2 x = fma2(make_float2(sa, sb), sc, nm);
     if ((e & 7) < POLY_PAIRS_PER_8) {
       x = exp2_poly2(x);
@@ -191,7 +215,9 @@ H3B_DEV float exp_pack64(uint32_t* r, uint32_t* dst, int valid, float scale_log2
     dst[e] = pack_bf16x2(p.x, p.y);
   }
   const float2 t = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
-  return t.x + t.y;
+  float m = 0.0f;
+  if constexpr (MAX) m = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+  return make_float2(t.x + t.y, m);
 }
 
 // 12 warps = 3 per SM sub-partition: launched at 168 registers per thread,
@@ -215,20 +241,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < KST; ++s) {
-      mbar_init(&bars->k_full[s], 1);
-      mbar_init(&bars->k_empty[s], 1);
-    }
-    for (int s = 0; s < VST; ++s) {
-      mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->v_empty[s], 1);
-    }
+    for (int s = 0; s < KST; ++s) mbar_init(&bars->k_full[s], 1);
+    for (int s = 0; s < VST; ++s) mbar_init(&bars->v_full[s], 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->kv_free[i], 1);
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_half[i][0], 4);  // one arrival per softmax warp
       mbar_init(&bars->p_half[i][1], 4);
-      mbar_init(&bars->pv_done[i], 1);
     }
+    mbar_init(&bars->o_done, 1);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -259,22 +280,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_kv && ok; ++j) {
-        // Slot j%KST was last used by K_{j-KST}; its release is phase j/KST-1.
-        const int ks = j % KST;
-        if (j >= KST && !mbar_wait(&bars->k_empty[ks], ((j / KST) - 1) & 1, &g_status, 1, abort_flag)) {
+        // K_j reuses K_{j-2}'s slot and V_j reuses V_{j-3}'s: both were
+        // released by kv_free(j-2), phase (j-2)/2 of kv_free[j % 2].  Its next
+        // phase, kv_free(j), needs K_j and V_j, so the wait is at most one
+        // phase behind.
+        if (j >= 2 && !mbar_wait(&bars->kv_free[j & 1], ((j - 2) >> 1) & 1, &g_status, 1, abort_flag)) {
           ok = false;
           break;
         }
+        const int ks = j % KST;
         mbar_arrive_expect_tx(&bars->k_full[ks], KV_TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sK + ks * KV_TILE_BYTES + h * KV_HALF_BYTES, &tm_k, h * 64, j * BKV, head,
                       &bars->k_full[ks]);
         issued_k = j + 1;
         const int vs = j % VST;
-        if (j >= VST && !mbar_wait(&bars->v_empty[vs], ((j / VST) - 1) & 1, &g_status, 2, abort_flag)) {
-          ok = false;
-          break;
-        }
         mbar_arrive_expect_tx(&bars->v_full[vs], KV_TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sV + vs * KV_TILE_BYTES + h * KV_HALF_BYTES, &tm_v, h * 64, j * BKV, head,
@@ -297,79 +317,76 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       bool ok = mbar_wait<true>(&bars->q_full, 0, &g_status, 3, abort_flag);
       tc_fence_after();
-      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + Q_TILE_BYTES)};
-      auto wait_k = [&](int j) -> uint32_t {
-        if (!mbar_wait<true>(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return 0u;
+      // k_full[j % 2] completes once per use of the slot; its next phase is
+      // K_{j+2}, loaded only after kv_free(j), which this thread commits
+      // later (behind S_0(j+1)): one phase behind.  Likewise v_full[j % 3]
+      // (next: V_{j+3}, after kv_free(j+1)).  K_{j+1} is waited for in
+      // iteration j, after kv_free(j-1) released the slot it is loaded into.
+      auto wait_k = [&](int j) -> bool {
+        if (!mbar_wait<true>(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return false;
         tc_fence_after();
-        return smem_u32(sK + (j % KST) * KV_TILE_BYTES);
+        return true;
       };
-      auto wait_v = [&](int j) -> uint32_t {
-        if (!mbar_wait<true>(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return 0u;
+      auto wait_v = [&](int j) -> bool {
+        if (!mbar_wait<true>(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return false;
         tc_fence_after();
-        return smem_u32(sV + (j % VST) * KV_TILE_BYTES);
+        return true;
       };
-      // S_i = Q_i K^T (fresh accumulator), then publish it.
-      auto issue_s = [&](int i, uint32_t k_addr) {
+      // S_i = Q_i K_j^T (fresh accumulator), then publish it.  K-major Q/K
+      // tiles advance 32 bytes (encoded 2) per 16-wide K step inside a
+      // 64-column half and a half tile (16 KB) every 4 steps: a descriptor
+      // step moves only the start-address field (desc_add_lo).
+      auto issue_s = [&](int i, int j) {
         const uint32_t d = tmem + s_col(i);
+        const uint64_t qd = sdesc_kmajor_sw128(smem_u32(sQ + i * Q_TILE_BYTES));
+        const uint64_t kd = sdesc_kmajor_sw128(smem_u32(sK + (j % KST) * KV_TILE_BYTES));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t ad = sdesc_kmajor_sw128(q_addr[i] + (kk >> 2) * Q_HALF_BYTES) + (kk & 3) * 2;
-          const uint64_t bd = sdesc_kmajor_sw128(k_addr + (kk >> 2) * KV_HALF_BYTES) + (kk & 3) * 2;
-          mma_f16_ss(d, ad, bd, IDESC_S, kk > 0);
+          const uint32_t step = static_cast<uint32_t>((kk >> 2) * (Q_HALF_BYTES >> 4) + (kk & 3) * 2);
+          mma_f16_ss(d, desc_add_lo(qd, step), desc_add_lo(kd, step), IDESC_S, kk > 0);
         }
         tc_commit(&bars->s_full[i]);
       };
       // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  Each
       // p_half[i][h] completes once per tile; the softmax cannot arrive for
       // j+1 before S_i(j+1), which is issued after these waits, so each wait
-      // is one phase behind.
-      // P is published in two halves (K/V rows 0-63, 64-127) so the first
-      // half of P.V runs while the softmax computes the second.
-      auto issue_pv = [&](int i, int j, uint32_t v_addr) -> bool {
+      // is one phase behind.  P is published in two halves (K/V rows 0-63,
+      // 64-127) so the first half of P.V runs while the softmax computes the
+      // second.  The MN-major V tile advances 2048 bytes per 16 keys.
+      auto issue_pv = [&](int i, int j) -> bool {
         const uint32_t p_tmem = tmem + s_col(i);
         const uint32_t o_tmem = tmem + o_col(i);
+        const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(sV + (j % VST) * KV_TILE_BYTES), KV_HALF_BYTES, 1024);
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait<true>(&bars->p_half[i][h], j & 1, &g_status, 7, abort_flag)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-            const uint64_t bd = sdesc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF_BYTES, 1024);
-            mma_f16_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 4 * h; kk < 4 * h + 4; ++kk)
+            mma_f16_ts(o_tmem, p_tmem + kk * 8, desc_add_lo(vd, static_cast<uint32_t>(kk * (2048 >> 4))),
+                       IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&bars->pv_done[i]);
         return true;
       };
-      uint32_t k_addr = ok ? wait_k(0) : 0u;
-      ok = k_addr != 0u;
+      ok = ok && wait_k(0);
       if (ok) {
-        issue_s(0, k_addr);
-        issue_s(1, k_addr);
-        tc_commit(&bars->k_empty[0]);
+        issue_s(0, 0);
+        issue_s(1, 0);
       }
-      uint32_t v_prev = ok ? wait_v(0) : 0u;
-      ok = ok && v_prev != 0u && issue_pv(0, 0, v_prev);
+      ok = ok && wait_v(0) && (n_kv == 1 || wait_k(1)) && issue_pv(0, 0);
       for (int j = 1; j < n_kv && ok; ++j) {
-        k_addr = wait_k(j);
-        if (k_addr == 0u) {
+        issue_s(0, j);                          // behind PV0(j-1) in the pipe
+        tc_commit(&bars->kv_free[(j - 1) & 1]);  // K_{j-1} and V_{j-2} no longer read
+        if (!issue_pv(1, j - 1)) {              // PV1(j-1)
           ok = false;
           break;
         }
-        issue_s(0, k_addr);                       // behind PV0(j-1) in the pipe
-        if (!issue_pv(1, j - 1, v_prev)) {        // PV1(j-1)
-          ok = false;
-          break;
-        }
-        tc_commit(&bars->v_empty[(j - 1) % VST]);  // V_{j-1} fully consumed
-        issue_s(1, k_addr);                       // behind PV1(j-1)
-        tc_commit(&bars->k_empty[j % KST]);
-        v_prev = wait_v(j);
-        if (v_prev == 0u || !issue_pv(0, j, v_prev)) {
+        issue_s(1, j);                          // behind PV1(j-1)
+        if (!wait_v(j) || (j + 1 < n_kv && !wait_k(j + 1)) || !issue_pv(0, j)) {
           ok = false;
           break;
         }
       }
-      if (ok && issue_pv(1, n_kv - 1, v_prev)) tc_commit(&bars->v_empty[(n_kv - 1) % VST]);
+      if (ok && issue_pv(1, n_kv - 1)) tc_commit(&bars->o_done);
       tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
     }
@@ -398,57 +415,72 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool full = valid >= BKV;  // uniform across the warp (same tile)
       // One TMEM round trip: all 128 columns in flight, one wait.
       uint32_t r[128];
+      auto load_s = [&]() {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32p(s_tmem + c * 32, r + 32 * c);
-      tmem_wait_fence<4>(r);
-      if (!full) {  // last K/V tile only (warp-uniform): padding columns -> -inf
+        for (int c = 0; c < 4; ++c) tmem_ld32p(s_tmem + c * 32, r + 32 * c);
+        tmem_wait_fence<4>(r);
+        if (!full) {  // last K/V tile only (warp-uniform): padding columns -> -inf
 #pragma unroll
-        for (int e = 0; e < 128; ++e)
-          if (e >= valid) r[e] = __float_as_uint(-INFINITY);
-      }
-      const float row_max = fmaxf(row_max64<false>(r, BKV), row_max64<false>(r + 64, BKV));
-      const float m_tile = row_max * args.scale_log2;
-      float m_use = m_run;
-      bool rescale = false;
-      if (m_tile > m_run + RESCALE_THRESHOLD) {
-        m_use = m_tile;
-        rescale = true;
-      }
-      // O correction first: O must be rescaled before P_i(j).V starts.  It
-      // runs warp-uniformly: tcgen05.ld/st are .sync.aligned and warp_wait
-      // shuffles over the full warp, so a per-row branch here would deadlock
-      // the warp.  Rows that need no rescale use factor 1.
-      if (__any_sync(0xffffffffu, rescale)) {
-        const float factor = rescale ? fast_exp2(m_run - m_use) : 1.0f;  // 0 on the first tile
-        l_run = l_run * factor;
-        if (j > 0) {
-          // O_i holds P.V of tiles < j.  The commit that published S_i(j)
-          // already covered PV_i(j-1); the wait (phase j-1, with phase j-2
-          // complete before S_i(j-1) was read) only formalises that.
-          if (!warp_wait(&bars->pv_done[wg], (j - 1) & 1, 21, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32p(o_tmem + c * 32, o);
-            tmem_wait_fence<1>(o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-            tmem_st32(o_tmem + c * 32, o);
-          }
+          for (int e = 0; e < 128; ++e)
+            if (e >= valid) r[e] = __float_as_uint(-INFINITY);
         }
-        if (rescale) m_run = m_use;
+      };
+      load_s();
+      // After the first tile, half 0 is exponentiated against the running
+      // max straight away and the tile's max is found alongside.  Only if a
+      // row's max exceeds the running max by more than the threshold (rare
+      // after the first tiles) does the warp reload S from TMEM — P has not
+      // been written over it yet — and take the rescaling path.
+      float m_use = m_run;
+      float sum = 0.0f;
+      bool slow = j == 0;
+      if (!slow) {
+        const float2 sm = exp_pack64<false, true>(r, r, BKV, args.scale_log2, -m_run);
+        slow = __any_sync(0xffffffffu, sm.y * args.scale_log2 > m_run + RESCALE_THRESHOLD);
+        if (slow) {
+          load_s();
+        } else {
+          sum = sm.x;
+        }
+      }
+      if (slow) {
+        const float row_max = fmaxf(row_max64<false>(r, BKV), row_max64<false>(r + 64, BKV));
+        const float m_tile = row_max * args.scale_log2;
+        bool rescale = false;
+        if (m_tile > m_run + RESCALE_THRESHOLD) {
+          m_use = m_tile;
+          rescale = true;
+        }
+        // O correction first: O must be rescaled before P_i(j).V starts.  It
+        // runs warp-uniformly: tcgen05.ld/st are .sync.aligned and warp_wait
+        // shuffles over the full warp, so a per-row branch here would
+        // deadlock the warp.  Rows that need no rescale use factor 1.
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float factor = rescale ? fast_exp2(m_run - m_use) : 1.0f;  // 0 on the first tile
+          l_run = l_run * factor;
+          if (j > 0) {
+            // O_i holds P.V of tiles < j: the commit that published S_i(j)
+            // also covered PV_i(j-1), and PV_i(j) waits for P_i(j) below.
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o[32];
+              tmem_ld32p(o_tmem + c * 32, o);
+              tmem_wait_fence<1>(o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+              tmem_st32(o_tmem + c * 32, o);
+            }
+          }
+          if (rescale) m_run = m_use;
+        }
+        sum = exp_pack64<false>(r, r, BKV, args.scale_log2, -m_use).x;
       }
       // P = exp2(s*scale - m) as packed bf16, published half by half: half h
       // (K/V rows 64h..64h+63) lands in columns 32h..32h+31 over S columns
       // already consumed.
-      float sum = 0.0f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        sum += exp_pack64<false>(r + 64 * h, r + 32 * h, BKV, args.scale_log2, -m_use);
+        if (h == 1) sum += exp_pack64<false>(r + 64, r + 32, BKV, args.scale_log2, -m_use).x;
         tmem_st32(s_tmem + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * h));
         tc_wait_st();
         tc_fence_before();
@@ -457,9 +489,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       l_run += sum;
     }
-    // ---- epilogue: O / l -> bf16 rows.  The last P.V is phase n_kv-1; phase
-    // n_kv-2 completed before S_i(n_kv-1) was published, so one phase behind.
-    if (ok && warp_wait(&bars->pv_done[wg], (n_kv - 1) & 1, 23, abort_flag)) {
+    // ---- epilogue: O / l -> bf16 rows once the last P.V of both tiles is
+    // complete (o_done has a single phase).
+    if (ok && warp_wait(&bars->o_done, 0, 23, abort_flag)) {
       tc_fence_after();
       const int q_row = q0 + wg * BQ + row;
       const float inv_l = 1.0f / l_run;

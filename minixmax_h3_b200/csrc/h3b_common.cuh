@@ -422,6 +422,15 @@ H3B_DEV uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_
          (static_cast<uint64_t>(sbo_bytes >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// Advances a shared-memory descriptor by `delta` (bytes >> 4) in its start
+// address field: one 32-bit add on the low word.  Valid while the resulting
+// address stays inside the same operand allocation below 256 KB of shared
+// memory, where the 14-bit field cannot carry into the next field.
+H3B_DEV uint64_t desc_add_lo(uint64_t d, uint32_t delta) {
+  const uint32_t lo = static_cast<uint32_t>(d) + delta;
+  return (d & 0xFFFFFFFF00000000ull) | lo;
+}
+
 // Instruction descriptors (kind::f16 / kind::i8 share this format).
 //  bits [4,6) D format (1 = f32, 2 = s32); [7,10) A format; [10,13) B format;
 //  15 / 16 A / B major (0 = K, 1 = MN); [17,23) N>>3; [24,29) M>>4.
