@@ -1,7 +1,7 @@
 """Single-kernel cases for profiling and timing sweeps.
 
     python -m minixmax_h3_b200.kernel_cases attention --seq 131072 --heads 3
-    python -m minixmax_h3_b200.kernel_cases gemm_nvfp4 --m 8192 --n 9216 --k 3072
+    python -m minixmax_h3_b200.kernel_cases gemm_nvfp4 --m 8192 --n 9216 --k 3072 [--epi gelu]
     python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
     python -m minixmax_h3_b200.kernel_cases gemm_sweep --warmup 3 --iters 20   # cfg 2 + cfg 3 shapes, M 32768
     python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
@@ -44,20 +44,27 @@ def _time(fn, warmup: int, iters: int) -> float:
 SWEEP_KN = ((3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072))
 
 
-def _gemm(case: str, m: int, n: int, k: int, warmup: int, iters: int, g, dev) -> dict:
+EPILOGUES = {"store": ops.EPI_STORE, "gelu": ops.EPI_GELU, "gate_res": ops.EPI_GATE_RES}
+
+
+def _gemm(case: str, m: int, n: int, k: int, warmup: int, iters: int, g, dev, epi: str = "store") -> dict:
     x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
     w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    kw: dict = {"epilogue": EPILOGUES[epi], "out": out}
+    if epi == "gate_res":  # out += gate[row_sel] * y, adaLN rows 0/1 as in the block
+        kw.update(resid=out, gate=(0.1 * torch.randn(2, n, generator=g, device=dev)).to(torch.bfloat16),
+                  row_sel=(torch.arange(m, device=dev) < 512).to(torch.int32))
     if case == "gemm_nvfp4":
         xa, wq = ops.quant_nvfp4(x), ops.quant_nvfp4(w)
-        ms = _time(lambda: ops.gemm_nvfp4(xa, wq, out=out), warmup, iters)
+        ms = _time(lambda: ops.gemm_nvfp4(xa, wq, **kw), warmup, iters)
     else:
         q, xs = ops.quant_i8_rows(x)
         wq = torch.randint(-128, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
         ws = torch.rand(n, device=dev, generator=g) * 1e-3
-        ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, out=out), warmup, iters)
+        ms = _time(lambda: ops.gemm_i8(q, xs, wq, ws, **kw), warmup, iters)
     flops = 2.0 * m * n * k
-    return {"m": m, "n": n, "k": k, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
+    return {"m": m, "n": n, "k": k, "epilogue": epi, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
 
 
 def main() -> None:
@@ -72,6 +79,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=3072)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--iters", type=int, default=2)
+    ap.add_argument("--epi", choices=sorted(EPILOGUES), default="store", help="GEMM epilogue")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
@@ -83,13 +91,13 @@ def main() -> None:
         flops = 4.0 * a.seq * a.seq * 128 * a.heads
         rec.update(seq=a.seq, heads=a.heads, ms=ms, tflops=flops / ms / 1e9, flops=flops)
     elif a.case in ("gemm_nvfp4", "gemm_i8"):
-        rec.update(_gemm(a.case, a.m, a.n, a.k, a.warmup, a.iters, g, dev))
+        rec.update(_gemm(a.case, a.m, a.n, a.k, a.warmup, a.iters, g, dev, a.epi))
     elif a.case == "gemm_sweep":
         # BASELINE cfg 2 / cfg 3: M = 32768 tokens, (K, N) of the four projections
         m = a.m if a.m != ap.get_default("m") else 32768
         for case in ("gemm_i8", "gemm_nvfp4"):
             for k, n in SWEEP_KN:
-                print(json.dumps({"case": case, **_gemm(case, m, n, k, a.warmup, a.iters, g, dev)}), flush=True)
+                print(json.dumps({"case": case, **_gemm(case, m, n, k, a.warmup, a.iters, g, dev, a.epi)}), flush=True)
         return
     elif a.case == "qk_rope":
         # q and k views of a packed [S, 3, H, 128] QKV buffer, in place

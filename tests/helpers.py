@@ -24,7 +24,11 @@ def assert_close_bf16(got: torch.Tensor, want: torch.Tensor, max_abs: float = 2e
     g = got.detach().float().cpu().reshape(-1)
     w = want.detach().float().cpu().reshape(-1)
     assert torch.isfinite(g).all(), "non-finite output"
-    err = ((g - w).abs() / w.abs().clamp(min=1.0)).max().item()
+    diff = (g - w).abs()
+    err = (diff / w.abs().clamp(min=1.0)).max().item()
+    raw = diff.max().item()
     cos = torch.nn.functional.cosine_similarity(g.double(), w.double(), dim=0).item()
-    assert err <= max_abs and cos >= min_cos, f"scaled max_abs={err:.4g} (<= {max_abs}) cos={cos:.6f} (>= {min_cos})"
-    return err, cos
+    assert err <= max_abs and cos >= min_cos, (
+        f"scaled max_abs={err:.4g} (<= {max_abs}) cos={cos:.6f} (>= {min_cos}); raw max_abs={raw:.4g}, "
+        f"{int((diff > 2e-2).sum())} of {diff.numel()} elements above an absolute 2e-2")
+    return err, cos, raw
