@@ -17,12 +17,16 @@
 //               launch) the single-thread MMA issuer.  tcgen05.commit (to
 //               both CTAs of a pair) releases smem slots and publishes
 //               finished accumulators.
-//   warps 2-5   epilogue of this CTA's 128 accumulator rows: tcgen05.ld
+//   warps 2-9   epilogue of this CTA's 128 accumulator rows, two warps per
+//               TMEM lane quadrant (a warp reaches only the lanes of quadrant
+//               warp % 4) taking alternate 32-column chunks: tcgen05.ld
 //               32x32b (one output row per thread), fp32 dequant/bias and
 //               GELU / SwiGLU / gate-residual / seq->head scatter, bf16
 //               blocks staged in 64B-swizzled shared memory and written by
 //               TMA stores; each warp releases the accumulator to the leader.
-//   warps 6-13  (NVFP4) scale writers, two per TMEM lane quadrant (a warp
+//               (With one warp per quadrant, a GELU or gate-residual epilogue
+//               outlasted the MMAs of a K = 3072 tile.)
+//   warps 10-17 (NVFP4) scale writers, two per TMEM lane quadrant (a warp
 //               reaches only the lanes of quadrant warp % 4), taking even
 //               and odd slabs: each loads its slab's scales from shared
 //               memory into registers ahead of time, stores them into its 32
@@ -61,7 +65,8 @@ constexpr int MAX_STAGES = 6;
 constexpr int A_BYTES = BM * 128;  // one 128-byte K slab of A
 constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
 constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
-constexpr int EPI_THREADS = 128;
+constexpr int EPI_THREADS = 256;  // two epilogue warps per TMEM lane quadrant
+constexpr int EPI_WARPS = EPI_THREADS / 32;
 constexpr int SF_THREADS = 256;  // NVFP4: two scale writer warps per TMEM lane quadrant (even / odd slabs)
 constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 staging buffer
 constexpr int SF_SLOTS = 2;               // NVFP4 scale slots in TMEM, one K slab each
@@ -149,7 +154,7 @@ struct __align__(8) Barriers {
 template <int KIND, int PAIR>
 constexpr size_t smem_bytes() {
   return 1024 /*alignment slack*/ + static_cast<size_t>(Cfg<KIND, PAIR>::STAGES) * Cfg<KIND, PAIR>::STAGE_BYTES +
-         4 * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
+         EPI_WARPS * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
 }
 static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
                   smem_bytes<KIND_I8, 1>() <= 227 * 1024,
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
   uint8_t* sSFA = sB + STAGES * C::B_BYTES;             // used by KIND_NVF4 only
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
   uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;       // 4 warps x 2 staging buffers, 1024-aligned
-  Barriers* bars = reinterpret_cast<Barriers*>(sOut + 4 * 2 * OUT_STAGE_BYTES);
+  Barriers* bars = reinterpret_cast<Barriers*>(sOut + EPI_WARPS * 2 * OUT_STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      mbar_init(&bars->acc_empty[b], 4 * PAIR);  // one arrival per epilogue warp of each CTA
+      mbar_init(&bars->acc_empty[b], EPI_WARPS * PAIR);  // one arrival per epilogue warp of each CTA
     }
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
@@ -437,7 +442,8 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    uint8_t* out_stage = sOut + quad * 2 * OUT_STAGE_BYTES;
+    const int half = (warp - 2) / 4;        // the quadrant's two warps take alternate 32-column chunks
+    uint8_t* out_stage = sOut + (warp - 2) * 2 * OUT_STAGE_BYTES;
     float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
     int stage_seq = 0;                      // alternates this warp's two staging buffers
@@ -465,6 +471,8 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       if (args.epilogue == H3B_EPI_GATE_RES && args.row_sel != nullptr && row_ok) gate_row = args.row_sel[row];
       const __nv_bfloat16* gate_r = args.gate + static_cast<int64_t>(gate_row < 0 ? 0 : gate_row) * args.gate_ld;
       const float gmul = gate_row < 0 ? 0.0f : 1.0f;  // rows outside every segment keep resid
+      // 16-byte gate loads when the table and its row pitch allow them
+      const bool gate_vec = ((reinterpret_cast<uintptr_t>(args.gate) | static_cast<uintptr_t>(args.gate_ld * 2)) & 15u) == 0;
       float row_scale = 1.0f;
       if constexpr (KIND == KIND_I8) {
         if (args.out_mode != OUT_I32 && row_ok) row_scale = args.xs[row];
@@ -523,14 +531,14 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       if (args.epilogue == H3B_EPI_SWIGLU) {
         // Column pair p: gate rows n0+64p .. +31 and up rows n0+64p+32 .. +63
         // of the interleaved weight -> output columns (n0 + 64p)/2 .. +31.
-        for (int p = 0; p < BN / 64; ++p) {
+        for (int p = half; p < BN / 64; p += 2) {
           uint32_t rg[32], ru[32];
           tmem_ld32p(t_row + p * 64, rg);
           tmem_ld32p(t_row + p * 64 + 32, ru);
           tc_wait_ld();
           reg_fence32(rg);
           reg_fence32(ru);
-          if (p == BN / 64 - 1) release_acc(buf);
+          if (p + 2 >= BN / 64) release_acc(buf);  // this warp's last pair
           const int gcol = n0 + p * 64;
           if (gcol >= args.n) continue;  // warp-uniform
           float v[32];
@@ -545,11 +553,11 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         }
         continue;
       }
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld32p(t_row + c * 32, r);
         tmem_wait_fence<1>(r);
-        if (c == BN / 32 - 1) release_acc(buf);
+        if (c + 2 >= BN / 32) release_acc(buf);  // this warp's last chunk
         const int col0 = n0 + c * 32;
         if (col0 >= args.n) continue;  // warp-uniform: the whole chunk is past the last column
         if (args.out_mode == OUT_I32) {
@@ -574,10 +582,20 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
           for (int j = 0; j < 32; j += 8) {
             const uint4 rv = *reinterpret_cast<const uint4*>(res + j);
             const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+            uint32_t gw[4];
+            if (gate_vec) {  // eight gate values in one 16-byte load
+              const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate_r + col0 + j));
+              gw[0] = gv.x, gw[1] = gv.y, gw[2] = gv.z, gw[3] = gv.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                gw[e] = static_cast<uint32_t>(__bfloat16_as_ushort(gate_r[col0 + j + 2 * e])) |
+                        (static_cast<uint32_t>(__bfloat16_as_ushort(gate_r[col0 + j + 2 * e + 1])) << 16);
+            }
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float g0 = __bfloat162float(gate_r[col0 + j + 2 * e]) * gmul;
-              const float g1 = __bfloat162float(gate_r[col0 + j + 2 * e + 1]) * gmul;
+              const float g0 = bf16lo_to_f32(gw[e]) * gmul;
+              const float g1 = bf16hi_to_f32(gw[e]) * gmul;
               v[j + 2 * e] = __fadd_rn(bf16lo_to_f32(rw[e]), __fmul_rn(v[j + 2 * e], g0));
               v[j + 2 * e + 1] = __fadd_rn(bf16hi_to_f32(rw[e]), __fmul_rn(v[j + 2 * e + 1], g1));
             }
