@@ -47,11 +47,13 @@ METRIC = "DiT-block tokens/s"
 # query rows of one head against all keys (about 10 s of CPU work on 16 cores)
 REF_TOKENS, REF_Q_ROWS = 4096, 512
 WARM_TOKENS, WARM_Q_ROWS = 1024, 128  # untimed warm-up sample
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention
-# launch over ONE head at the bench's S = 498,272 (small-case ncu capture,
-# profiles/attention_kernel_S498272_H1_dram.md); a launch over H heads moves
-# H times that, since every wave of CTAs works on one head at a time.
-ATTN_DRAM_BYTES_PER_HEAD = None
+# roofline.traffic stays null: small-case ncu captures at the bench's S =
+# 498,272 (profiles/attention_kernel_S498272_H1-4_dram.md) show DRAM bytes per
+# head growing with the number of heads in a launch (3.7 / 4.6 / 9.5 GB per head
+# for 1 / 2 / 4 heads: the CTAs drift apart along each head's 255 MB of K/V over
+# the waves), so scaling a small capture by heads would understate a full launch.
+ATTN_DRAM_NOTE = ("not proportional to heads: 3.73 / 4.57 / 9.47 GB read per head in 1 / 2 / 4-head "
+                  "launches at this S (profiles/attention_kernel_S498272_H1-4_dram.md); no full-size capture")
 UNIT = "block-tokens/s"
 WORKLOAD = ("cfg5: one denoising step of 4 DiT blocks, hidden 3072, 24x128 heads, GELU MLP 12288, NVFP4 W4A4 "
             "linears, 512 text (dim 4096) + 497760 video tokens (t61 x h68 x w120) = 498272-token joint attention, "
@@ -461,7 +463,6 @@ def run_gpu(args) -> None:
     else:
         statuses = [status]
     if rank == 0:
-        traffic = None if ATTN_DRAM_BYTES_PER_HEAD is None else ATTN_DRAM_BYTES_PER_HEAD * (HEADS // ws)
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
             torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
@@ -479,8 +480,8 @@ def run_gpu(args) -> None:
                     "d2h_bytes_per_step": d2h},
             "roofline": {"kernel": "attention_kernel (tcgen05 flash attention)", "bound": "tensor",
                          "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s", "frac": achieved / pk["bf16"],
-                         "peak_kind": f"bf16 sustained ({pk['source']})", "traffic": traffic,
-                         "traffic_kind": "ncu DRAM bytes of a 1-head launch at this S, times heads per rank",
+                         "peak_kind": f"bf16 sustained ({pk['source']})", "traffic": None,
+                         "traffic_note": ATTN_DRAM_NOTE,
                          "launch_ms": attn_ms, "flops_per_launch": attn_flops},
             "gemm_roofline": {"kernel": f"gemm_kernel NVFP4 ({g_name}: M={g_m} N={g_n} K={g_k})", "format": g_fmt,
                               "bound": "tensor", "achieved": g_flops / (g_ms / g_count * 1e-3) / 1e12,

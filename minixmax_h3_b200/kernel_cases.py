@@ -1,6 +1,6 @@
 """Single-kernel cases for profiling and timing sweeps.
 
-    python -m minixmax_h3_b200.kernel_cases attention --seq 131072 --heads 3
+    python -m minixmax_h3_b200.kernel_cases attention --seq 131072 --heads 3 [--layout packed]
     python -m minixmax_h3_b200.kernel_cases gemm_nvfp4 --m 8192 --n 9216 --k 3072 [--epi gelu]
     python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
     python -m minixmax_h3_b200.kernel_cases gemm_sweep --warmup 3 --iters 20   # cfg 2 + cfg 3 shapes, M 32768
@@ -80,13 +80,19 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--iters", type=int, default=2)
     ap.add_argument("--epi", choices=sorted(EPILOGUES), default="store", help="GEMM epilogue")
+    ap.add_argument("--layout", choices=["separate", "packed"], default="separate",
+                    help="attention: separate [S, H, 128] tensors or views of a packed [S, 3, H, 128] QKV")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     rec: dict = {"case": a.case}
     if a.case == "attention":
-        q, k, v = (torch.randn(a.seq, a.heads, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
-        o = torch.empty_like(q)
+        if a.layout == "packed":  # q/k/v as views of one [S, 3, H, 128] projection output, as in a block
+            qkv = torch.randn(a.seq, 3, a.heads, 128, generator=g, device=dev).to(torch.bfloat16)
+            q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+        else:
+            q, k, v = (torch.randn(a.seq, a.heads, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        o = torch.empty(a.seq, a.heads, 128, dtype=torch.bfloat16, device=dev)
         ms = _time(lambda: ops.attention(q, k, v, out=o), a.warmup, a.iters)
         flops = 4.0 * a.seq * a.seq * 128 * a.heads
         rec.update(seq=a.seq, heads=a.heads, ms=ms, tflops=flops / ms / 1e9, flops=flops)
