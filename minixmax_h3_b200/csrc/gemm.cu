@@ -4,51 +4,60 @@
 //                  y = acc * xs[m] * ws[n] (+ bias[n])  — the semantics of
 //                  torch_npu.npu_quant_matmul at ops/int8_convrot.py:86-93.
 //   NVFP4 (W4A4):  kind::mxf4nvf4.block_scale.block16, e2m1 operands with one
-//                  ue4m3 scale per 16 elements written into TMEM by four
+//                  ue4m3 scale per 16 elements written into TMEM by
 //                  scale-writer warps, epilogue y = acc * a_gs * w_gs (+ bias[n]).
 //
-// Structure (persistent, one CTA per SM; INT8 GEMMs with M > 128 work in
-// clusters of two CTAs on 256 x BN tiles with cta_group::2 MMAs):
+// Structure (persistent, one CTA per SM; every GEMM with M > 128 works in
+// clusters of two CTAs on 256 x BN tiles with cta_group::2 MMAs; M <= 128
+// keeps single-CTA 128 x BN tiles):
 //   warp 0      TMA producer: this CTA's 128 rows of A, its BN/PAIR rows of B
-//               (+ scale factors) into a 4- or 6-deep smem ring.  In a pair,
-//               both CTAs' copies complete on the leader's full barrier,
-//               which only the leader arms (for both CTAs' bytes).
+//               (+ scale factors) into a 4-, 5- or 6-deep smem ring.  In a
+//               pair, both CTAs' A/B copies complete on the leader's full
+//               barrier, which only the leader arms (for both CTAs' bytes);
+//               NVFP4 scale bytes land on each CTA's own sf_ready barrier.
 //   warp 1      TMEM allocator; in the leader (the only CTA of a single-CTA
 //               launch) the single-thread MMA issuer.  tcgen05.commit (to
 //               both CTAs of a pair) releases smem slots and publishes
 //               finished accumulators.
-//   warps 2-9   epilogue of this CTA's 128 accumulator rows, two warps per
-//               TMEM lane quadrant (a warp reaches only the lanes of quadrant
-//               warp % 4) taking alternate 32-column chunks: tcgen05.ld
-//               32x32b (one output row per thread), fp32 dequant/bias and
-//               GELU / SwiGLU / gate-residual / seq->head scatter, bf16
-//               blocks staged in 64B-swizzled shared memory and written by
-//               TMA stores; each warp releases the accumulator to the leader.
-//               (With one warp per quadrant, a GELU or gate-residual epilogue
-//               outlasted the MMAs of a K = 3072 tile.)
-//   warps 10-17 (NVFP4) scale writers, two per TMEM lane quadrant (a warp
-//               reaches only the lanes of quadrant warp % 4), taking even
-//               and odd slabs: each loads its slab's scales from shared
-//               memory into registers ahead of time, stores them into its 32
-//               TMEM lanes with tcgen05.st and arrives on the slab's full
-//               barrier, so the MMA thread waits once per slab and issues
-//               nothing but MMAs.  (With one writer per quadrant, the ones
-//               sharing a scheduler with the producer or the MMA thread fell
-//               a slab behind and paced the pipe.)
+//   epilogue    8 warps (2-9; 8-15 in an NVFP4 pair) for this CTA's 128
+//               accumulator rows, two per TMEM lane quadrant (a warp reaches
+//               only the lanes of quadrant warp % 4) taking alternate
+//               32-column chunks: tcgen05.ld 32x32b (one output row per
+//               thread), fp32 dequant/bias and GELU / SwiGLU / gate-residual /
+//               seq->head scatter, bf16 blocks staged in 64B-swizzled shared
+//               memory and written by TMA stores; each warp releases the
+//               accumulator to the leader.  (With one warp per quadrant, a
+//               GELU or gate-residual epilogue outlasted the MMAs of a
+//               K = 3072 tile.)  Each epilogue mode is its own kernel instance.
+//   writers     (NVFP4) scale writers (warps 10-17 single-CTA, two per TMEM
+//               lane quadrant on alternate slabs; warps 4-7 in a pair, one per
+//               quadrant): each loads its slab's scales from shared memory into
+//               registers, stores them into its 32 TMEM lanes with tcgen05.st
+//               and arrives on the slab's full barrier (the leader's, in a
+//               pair), so the MMA thread waits once per slab and issues
+//               nothing but MMAs.  (With one single-CTA writer per quadrant,
+//               the ones sharing a scheduler with the producer or the MMA
+//               thread fell a slab behind and paced the pipe.)
 // The single issuing thread is the MMA pipe's feeder: a block-scaled MMA
-// takes ~55 cycles to issue, a commit ~75 and a barrier poll ~80, so 4 NVFP4
-// MMAs of 128x192x64 per 384-cycle slab leave it no room for the 12 scale
-// copies (tcgen05.cp, ~45 cycles of issue each) a slab would need.
-// Accumulators are double-buffered in TMEM (BN columns apart), so the MMAs
-// of tile t+1 run while the epilogue drains tile t:
-//   INT8:  BN = 256.
-//   NVFP4: BN = 192, plus two 48-column scale slots at columns 384 and 432
-//          (slab it uses slot it&1; the writers refill it once the MMAs of
-//          slab it-2 have completed, seen through that slab's empty
-//          barrier).  A slot holds, per K-step j, 4 columns of A scales
-//          (the four-quadrant image of the blocked 128x4 atom: lane 32q+b,
-//          column 4j+a = scales of row 32a+b) and 8 columns of B scales
-//          (column 8j+i = scales of tile rows 32i+b in every quadrant).
+// takes ~55-75 cycles to issue, a commit ~60-75 and a barrier poll ~80, so 4
+// NVFP4 MMAs of 128x192x64 per 384-cycle slab leave it no room for the 12
+// scale copies (tcgen05.cp, ~45 cycles of issue each) a slab would need.
+// Accumulators in TMEM:
+//   INT8:        BN = 256, two accumulators (columns 0 and 256), so the MMAs
+//                of tile t+1 run while the epilogue drains tile t.
+//   NVFP4 1-CTA: BN = 192, two accumulators (0, 192), plus two 48-column
+//                scale slots at columns 384 and 432 (slab it uses slot it&1;
+//                the writers refill it once the MMAs of slab it-2 have
+//                completed, seen through that slab's empty barrier).
+//   NVFP4 pair:  BN = 256, one accumulator (0-255), five scale slots at
+//                256 + 48s (slab it uses slot it % 5, refilled after the MMAs
+//                of slab it-5); the epilogue reads its whole share into
+//                registers and releases the accumulator before computing.
+//   A slot holds, per K-step j, 4 columns of A scales (the four-quadrant image
+//   of the blocked 128x4 atom: lane 32q+b, column 4j+a = scales of row 32a+b)
+//   and 8 columns of B scales (column 8j+i = scales of tile rows 32i+b in
+//   every quadrant).  In a pair each CTA holds the A scales of its own rows
+//   and the B scales of all 256 tile rows.
 // Operands are K-major with the 128-byte swizzle.  No load uses cluster
 // multicast.  Every wait is bounded; both CTAs of a pair stay resident until
 // a final cluster barrier.
@@ -67,13 +76,21 @@ constexpr int SFA_BYTES = 2048;    // 128 rows x 16 scales (4 blocked chunks)
 constexpr int SFB_BYTES = 4096;    // two 128-row blocks x 16 scales
 constexpr int EPI_THREADS = 256;  // two epilogue warps per TMEM lane quadrant
 constexpr int EPI_WARPS = EPI_THREADS / 32;
-constexpr int SF_THREADS = 256;  // NVFP4: two scale writer warps per TMEM lane quadrant (even / odd slabs)
 constexpr int OUT_STAGE_BYTES = 32 * 64;  // one warp's 32 rows x 32 bf16 staging buffer
-constexpr int SF_SLOTS = 2;               // NVFP4 scale slots in TMEM, one K slab each
 constexpr int SF_SLOT_COLS = 48;          // 16 (A: 4 K-steps x 4) + 32 (B: 4 K-steps x 8)
 
 enum Kind { KIND_I8 = 0, KIND_NVF4 = 1 };
 enum OutMode { OUT_BF16 = 0, OUT_I32 = 1, OUT_SEQ2HEAD = 2 };
+// Epilogue specialisation of a kernel instance: the activation (H3B_EPI_*)
+// or the output form.  Each mode is its own instance so a kernel carries
+// only the epilogue code it runs (runtime selection among all of them left
+// every instance's code large enough to cost ~6 % in instruction fetch).
+enum EpiMode { EM_STORE = 0, EM_GELU = 1, EM_GATE_RES = 2, EM_SWIGLU = 3, EM_I32 = 4, EM_SEQ2HEAD = 5 };
+template <int EM>
+struct EpiOf {
+  static constexpr int epilogue = EM <= EM_SWIGLU ? EM : H3B_EPI_STORE;  // H3B_EPI_* values
+  static constexpr int out_mode = EM == EM_I32 ? OUT_I32 : (EM == EM_SEQ2HEAD ? OUT_SEQ2HEAD : OUT_BF16);
+};
 
 constexpr int MAX_PEERS = 8;
 struct PeerMaps {
@@ -107,30 +124,64 @@ struct GemmArgs {
 // 256 x BN tile with cta_group::2 MMAs issued by the leader (rank 0): each
 // CTA stages its 128 rows of A and BN/2 rows of B, and holds its 128 rows of
 // the accumulator, so each SM moves half as much B through shared memory.
+//
+// NVFP4 pairs (256 x 256 tiles) exist for shared-memory bandwidth: a 128x192
+// FP4 tile at full MMA rate reads ~107 B/clk of operands from shared memory
+// while TMA writes as many, against ~128 B/clk per SM; a pair's 128 rows of
+// A plus 128 of B per SM need half of that per FLOP, and its 4 MMAs per slab
+// take 512 cycles instead of 384, which leaves the single issuing thread room.
+// Two 256-column accumulators would fill TMEM, so an NVFP4 pair has one: the
+// epilogue reads its whole share into registers (192 per thread through
+// setmaxnreg) and releases it before computing, and five scale slots let
+// the writers run up to five slabs ahead of the MMAs.
 template <int KIND, int PAIR>
 struct Cfg {
-  static constexpr int BN = KIND == KIND_I8 ? 256 : 192;  // MMA N
+  static constexpr bool NVF4_PAIR = KIND == KIND_NVF4 && PAIR == 2;
+  static constexpr int BN = (KIND == KIND_I8 || PAIR == 2) ? 256 : 192;  // MMA N
   static constexpr int B_ROWS = BN / PAIR;                 // B rows staged by this CTA
   static constexpr int B_BYTES = B_ROWS * 128;
-  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
-  static constexpr int ACC_STRIDE = BN;        // TMEM columns between the two accumulators
-  static constexpr int SF_BASE = 2 * BN;       // NVFP4 scale slots follow the accumulators
+  static constexpr int STAGES = PAIR == 1 ? 4 : (NVF4_PAIR ? 5 : 6);
+  static constexpr int NACC = NVF4_PAIR ? 1 : 2;  // TMEM accumulators (double-buffered unless NVF4_PAIR)
+  static constexpr int ACC_STRIDE = BN;        // TMEM columns between the accumulators
+  static constexpr int SF_BASE = NACC * BN;    // NVFP4 scale slots follow the accumulators
+  static constexpr int SF_SLOTS = NVF4_PAIR ? 5 : 2;  // NVFP4 scale slots in TMEM, one K slab each
+  static constexpr int SF_WPQ = NVF4_PAIR ? 1 : 2;    // NVFP4 scale writer warps per TMEM lane quadrant
   static constexpr int TMEM_COLS = 512;
   static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
   // The leader's full barrier counts both CTAs' A and B bytes (and, for
-  // NVFP4, the four scale writers' arrivals); scale bytes land on sf_ready.
+  // NVFP4, one scale writer per quadrant of each CTA); scale bytes land on
+  // each CTA's own sf_ready.
   static constexpr int TX_BYTES = PAIR * (A_BYTES + B_BYTES);
-  static constexpr int FULL_ARRIVALS = KIND == KIND_NVF4 ? 1 + 4 : 1;  // the arm + one writer per quadrant
-  static constexpr int THREADS = 64 + EPI_THREADS + (KIND == KIND_NVF4 ? SF_THREADS : 0);
+  static constexpr int FULL_ARRIVALS = KIND == KIND_NVF4 ? 1 + 4 * PAIR : 1;  // the arm + the writers
+  // Warp roles: 0 TMA producer, 1 TMEM allocator + MMA issuer, then the
+  // epilogue and (NVFP4) the scale writers.  An NVFP4 pair aligns roles to
+  // warpgroups for setmaxnreg: warps 2-3 idle, 4-7 writers, 8-15 epilogue.
+  static constexpr int EPI_WARP0 = NVF4_PAIR ? 8 : 2;
+  static constexpr int SF_WARP0 = NVF4_PAIR ? 4 : 2 + EPI_WARPS;
+  static constexpr int SF_WARPS = KIND == KIND_NVF4 ? 4 * SF_WPQ : 0;
+  static constexpr int THREADS = NVF4_PAIR ? 512 : 64 + EPI_THREADS + 32 * SF_WARPS;
   static constexpr int K_PER_STAGE = KIND == KIND_I8 ? 128 : 256;  // elements per 128-byte slab
   static constexpr uint32_t IDESC = KIND == KIND_I8 ? idesc_s8_s32(BM * PAIR, BN) : idesc_nvf4(BM * PAIR, BN);
   static_assert(STAGES <= MAX_STAGES, "barrier arrays");
-  static_assert(KIND == KIND_I8 || PAIR == 1, "NVFP4 runs single-CTA tiles");
-  static_assert(2 * ACC_STRIDE <= TMEM_COLS, "accumulators exceed TMEM");
+  static_assert(NACC * ACC_STRIDE <= TMEM_COLS, "accumulators exceed TMEM");
   static_assert(KIND == KIND_I8 || SF_BASE + SF_SLOTS * SF_SLOT_COLS <= TMEM_COLS, "scale slots exceed TMEM");
+  // A writer waits for slab it - SF_SLOTS to release its slot on that slab's
+  // empty barrier; with SF_SLOTS <= STAGES that barrier cannot have moved on
+  // by another phase before this writer's own later arrival.
+  static_assert(KIND == KIND_I8 || SF_SLOTS <= STAGES, "scale slot reuse needs a stage per slot");
   static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 };
+
+// NVFP4 pair register split (setmaxnreg per warpgroup): launched at 128 per
+// thread (512 x 128), the control warpgroup (producer, MMA, two idle warps)
+// drops to 56, the scale writers to 72, and the two epilogue warpgroups rise
+// to 192 so each epilogue thread can hold its 128 accumulator columns.
+constexpr int PAIR_LAUNCH_REGS = 128;
+constexpr int REGS_CTL = 56;
+constexpr int REGS_SFW = 72;
+constexpr int REGS_EPI = 192;
+static_assert(4 * REGS_CTL + 4 * REGS_SFW + 8 * REGS_EPI <= 16 * PAIR_LAUNCH_REGS, "register split exceeds launch");
 
 // TMEM column of NVFP4 scale slot `slot` (A scales at +4j, B scales at
 // +16+8j for K-step j).
@@ -157,7 +208,7 @@ constexpr size_t smem_bytes() {
          EPI_WARPS * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
 }
 static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
-                  smem_bytes<KIND_I8, 1>() <= 227 * 1024,
+                  smem_bytes<KIND_I8, 1>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 2>() <= 227 * 1024,
               "shared memory budget");
 
 H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
@@ -175,7 +226,7 @@ H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* a
 // buffer must be 512-byte aligned.
 H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EM>
 __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ PeerMaps peers,
@@ -239,6 +290,10 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
+  // Under NVF4_PAIR each role branch opens with its warpgroup's setmaxnreg
+  // (one static instruction per warpgroup, executed by all of its warps).
+  if (warp < (C::NVF4_PAIR ? 4 : 2)) {
+   if constexpr (C::NVF4_PAIR) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTL));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // (no_loads: nothing is issued, so no copy is ever in flight and the
@@ -265,6 +320,26 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
             tma_load_2d_pair(sA + s * A_BYTES, &tmap_a, kb * 128, m0, full_l);
             tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_b, kb * 128, n0 + static_cast<int>(rank) * C::B_ROWS,
                              full_l);
+            if constexpr (KIND == KIND_NVF4) {
+              // This CTA's scales land in its own shared memory (own
+              // sf_ready): the A block of its 128 rows and both 128-row B
+              // blocks of the 256-row tile.  A block or a second B block past
+              // the last one is replaced by the tile's first (in bounds; the
+              // rows or columns it would scale are never stored).
+              const int64_t ncb = args.k / 64;
+              const int a_blocks = (args.m + BM - 1) / BM;
+              const int ab = mt * 2 + static_cast<int>(rank) < a_blocks ? mt * 2 + static_cast<int>(rank) : mt * 2;
+              const int nb0 = n0 / 128;
+              const int nb1 = (nb0 + 1) * 128 < args.n ? nb0 + 1 : nb0;
+              mbar_arrive_expect_tx(&bars->sf_ready[s], C::SF_STAGE_BYTES);
+              bulk_load(sSFA + s * SFA_BYTES, args.a_sf + ((static_cast<int64_t>(ab) * ncb) + kb * 4) * 512,
+                        SFA_BYTES, &bars->sf_ready[s]);
+              bulk_load(sSFB + s * SFB_BYTES, args.w_sf + ((static_cast<int64_t>(nb0) * ncb) + kb * 4) * 512,
+                        SFB_BYTES / 2, &bars->sf_ready[s]);
+              bulk_load(sSFB + s * SFB_BYTES + SFB_BYTES / 2,
+                        args.w_sf + ((static_cast<int64_t>(nb1) * ncb) + kb * 4) * 512, SFB_BYTES / 2,
+                        &bars->sf_ready[s]);
+            }
             continue;
           }
           mbar_arrive_expect_tx(&bars->full[s], C::TX_BYTES);
@@ -322,10 +397,13 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     if (lane == 0 && leader) {
       int it = 0;
       int local = 0;
+      // stage, its phase and the scale slot of slab `it`, kept as running
+      // counters (no division per slab in this latency-critical loop)
+      int s = 0, ph = 0, slot = 0;
       bool ok = true;
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters, ++local) {
-        const int buf = local & 1;
-        const int use = local >> 1;
+        const int buf = local % C::NACC;
+        const int use = local / C::NACC;
         if (use > 0 && !mbar_wait<false, PAIR == 2>(&bars->acc_empty[buf], (use - 1) & 1, &g_status, 2, abort_flag)) {
           ok = false;
           break;
@@ -333,8 +411,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int s = it % STAGES;
-          if (!mbar_wait<true>(&bars->full[s], (it / STAGES) & 1, &g_status, 3, abort_flag)) {
+          if (!mbar_wait<true>(&bars->full[s], static_cast<uint32_t>(ph), &g_status, 3, abort_flag)) {
             ok = false;
             break;
           }
@@ -351,18 +428,28 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
                 mma_i8_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, (kb | j) != 0);
             }
           } else {
-            // full[s] also means: this slab's scales are in TMEM slot it&1
-            const uint32_t sf_col = tmem_base + sf_slot_col<KIND, PAIR>(it & 1);
+            // full[s] also means: this slab's scales are in TMEM slot it % SF_SLOTS
+            const uint32_t sf_col = tmem_base + sf_slot_col<KIND, PAIR>(slot);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4, sf_col + 16 + j * 8,
-                          (kb | j) != 0);
+            for (int j = 0; j < 4; ++j) {
+              if constexpr (PAIR == 2)
+                mma_nvf4_ss_pair(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4,
+                                 sf_col + 16 + j * 8, (kb | j) != 0);
+              else
+                mma_nvf4_ss(d_tmem, adesc + 2 * j, bdesc + 2 * j, C::IDESC, sf_col + j * 4, sf_col + 16 + j * 8,
+                            (kb | j) != 0);
+            }
           }
           // stage reusable (in both CTAs) once these MMAs have read it
           if constexpr (PAIR == 2)
             tc_commit_pair_mc(&bars->empty[s], 0x3);
           else
             tc_commit(&bars->empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+          if (++slot == C::SF_SLOTS) slot = 0;
         }
         if (!ok) break;
         if constexpr (PAIR == 2)  // accumulator complete in both CTAs
@@ -377,8 +464,62 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         tc_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
     }
-  } else if (KIND == KIND_NVF4 && warp >= 2 + EPI_THREADS / 32) {
+  }
+  } else if (KIND == KIND_NVF4 && warp >= C::SF_WARP0 && warp < C::SF_WARP0 + C::SF_WARPS) {
     // ------------------------------------------------------ scale writers
+   if constexpr (C::NVF4_PAIR) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_SFW));
+    // Pair: one writer per quadrant and CTA, every slab, slot it % 5.  Each
+    // CTA's TMEM holds the A scales of its own 128 rows (the layout below)
+    // and the B scales of the whole 256-row tile: column 16+8j+i = tile rows
+    // 32i+b, i < 8, in every quadrant.  The slab's scales are read from
+    // shared memory right before they are stored: five slots of lead leave
+    // no need to prefetch.  The follower's writers arrive on the leader's
+    // full barrier.
+    const int quad = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int my_tiles = cluster < num_tiles ? (num_tiles - 1 - cluster) / n_clusters + 1 : 0;
+    const int total = my_tiles * nk;
+    bool ok = true;
+    for (int it = 0; it < total && ok; ++it) {
+      const int s = it % STAGES;
+      if (!warp_wait<true>(&bars->sf_ready[s], (it / STAGES) & 1, 7, abort_flag)) {
+        ok = false;
+        break;
+      }
+      uint32_t ra[16], rb[32];
+      const uint8_t* sfa = sSFA + s * SFA_BYTES + lane * 16;
+      const uint8_t* sfb = sSFB + s * SFB_BYTES + lane * 16;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 a4 = *reinterpret_cast<const uint4*>(sfa + j * 512);
+        const uint4 b0 = *reinterpret_cast<const uint4*>(sfb + j * 512);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(sfb + SFB_BYTES / 2 + j * 512);
+        ra[4 * j] = a4.x, ra[4 * j + 1] = a4.y, ra[4 * j + 2] = a4.z, ra[4 * j + 3] = a4.w;
+        rb[8 * j] = b0.x, rb[8 * j + 1] = b0.y, rb[8 * j + 2] = b0.z, rb[8 * j + 3] = b0.w;
+        rb[8 * j + 4] = b1.x, rb[8 * j + 5] = b1.y, rb[8 * j + 6] = b1.z, rb[8 * j + 7] = b1.w;
+      }
+      // slot it % 5 was last read by the MMAs of slab it-5
+      if (it >= C::SF_SLOTS && !warp_wait<true>(&bars->empty[(it - C::SF_SLOTS) % STAGES],
+                                                ((it - C::SF_SLOTS) / STAGES) & 1, 6, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR>(it % C::SF_SLOTS);
+      tmem_st16(t, ra);
+      tmem_st32(t + 16, rb);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&bars->full[s]);
+        else
+          mbar_arrive_remote(mapa_shared(smem_u32(&bars->full[s]), 0));
+      }
+    }
+   } else {
     // Warp q writes TMEM lanes 32q..32q+31 of slot it&1 for slab it:
     //   A part, column 4j+a: word a of row b of blocked chunk j (the four
     //     scales of A row 32a+b for K-step j; quadrant q reads column 4j+q);
@@ -438,12 +579,14 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       if (lane == 0) mbar_arrive(&bars->full[it % STAGES]);
       if (it + 2 < total) ok = load(it + 2);
     }
-  } else {
+   }
+  } else if (warp >= C::EPI_WARP0 && warp < C::EPI_WARP0 + EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
+    if constexpr (C::NVF4_PAIR) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPI));
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    const int half = (warp - 2) / 4;        // the quadrant's two warps take alternate 32-column chunks
-    uint8_t* out_stage = sOut + (warp - 2) * 2 * OUT_STAGE_BYTES;
+    const int half = (warp - C::EPI_WARP0) / 4;  // the quadrant's two warps take alternate 32-column chunks
+    uint8_t* out_stage = sOut + (warp - C::EPI_WARP0) * 2 * OUT_STAGE_BYTES;
     float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
     int stage_seq = 0;                      // alternates this warp's two staging buffers
@@ -452,15 +595,21 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if constexpr (PAIR == 2)
+        if constexpr (C::NVF4_PAIR) {
+          if (leader)
+            mbar_arrive(&bars->acc_empty[buf]);
+          else
+            mbar_arrive_remote(mapa_shared(smem_u32(&bars->acc_empty[buf]), 0));
+        } else if constexpr (PAIR == 2) {
           mbar_arrive_cluster(mapa_shared(smem_u32(&bars->acc_empty[buf]), 0));
-        else
+        } else {
           mbar_arrive(&bars->acc_empty[buf]);
+        }
       }
     };
     for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
-      const int buf = local & 1;
-      const int use = local >> 1;
+      const int buf = local % C::NACC;
+      const int use = local / C::NACC;
       if (!warp_wait(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
       tc_fence_after();
       const int m0 = ((tile / n_tiles) * PAIR + static_cast<int>(rank)) * BM;
@@ -468,14 +617,14 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
       const int row = m0 + row_in_tile;
       const bool row_ok = row < args.m;
       int gate_row = 0;
-      if (args.epilogue == H3B_EPI_GATE_RES && args.row_sel != nullptr && row_ok) gate_row = args.row_sel[row];
+      if (EpiOf<EM>::epilogue == H3B_EPI_GATE_RES && args.row_sel != nullptr && row_ok) gate_row = args.row_sel[row];
       const __nv_bfloat16* gate_r = args.gate + static_cast<int64_t>(gate_row < 0 ? 0 : gate_row) * args.gate_ld;
       const float gmul = gate_row < 0 ? 0.0f : 1.0f;  // rows outside every segment keep resid
       // 16-byte gate loads when the table and its row pitch allow them
       const bool gate_vec = ((reinterpret_cast<uintptr_t>(args.gate) | static_cast<uintptr_t>(args.gate_ld * 2)) & 15u) == 0;
       float row_scale = 1.0f;
       if constexpr (KIND == KIND_I8) {
-        if (args.out_mode != OUT_I32 && row_ok) row_scale = args.xs[row];
+        if (EpiOf<EM>::out_mode != OUT_I32 && row_ok) row_scale = args.xs[row];
       } else {
         row_scale = (*args.a_gs) * (*args.w_gs);
       }
@@ -516,7 +665,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (args.out_mode == OUT_SEQ2HEAD) {
+          if (EpiOf<EM>::out_mode == OUT_SEQ2HEAD) {
             const int part = ocol / args.hd, rem = ocol - part * args.hd;
             const int head = rem >> 7, d0 = rem & 127;
             const int dst = head / args.heads_per_rank, lh = head - dst * args.heads_per_rank;
@@ -528,39 +677,26 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         }
         ++stage_seq;
       };
-      if (args.epilogue == H3B_EPI_SWIGLU) {
-        // Column pair p: gate rows n0+64p .. +31 and up rows n0+64p+32 .. +63
-        // of the interleaved weight -> output columns (n0 + 64p)/2 .. +31.
-        for (int p = half; p < BN / 64; p += 2) {
-          uint32_t rg[32], ru[32];
-          tmem_ld32p(t_row + p * 64, rg);
-          tmem_ld32p(t_row + p * 64 + 32, ru);
-          tc_wait_ld();
-          reg_fence32(rg);
-          reg_fence32(ru);
-          if (p + 2 >= BN / 64) release_acc(buf);  // this warp's last pair
-          const int gcol = n0 + p * 64;
-          if (gcol >= args.n) continue;  // warp-uniform
-          float v[32];
+      // Column pair p: gate rows n0+64p .. +31 and up rows n0+64p+32 .. +63
+      // of the interleaved weight -> output columns (n0 + 64p)/2 .. +31.
+      auto swiglu_pair = [&](const uint32_t* rg, const uint32_t* ru, int p) {
+        const int gcol = n0 + p * 64;
+        if (gcol >= args.n) return;  // warp-uniform
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float g = bf16r(dequant(rg[j], gcol + j));
-            const float u = bf16r(dequant(ru[j], gcol + 32 + j));
-            const float sg = bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-            v[j] = __fmul_rn(sg, u);
-          }
-          store_block(v, gcol / 2);
+        for (int j = 0; j < 32; ++j) {
+          const float g = bf16r(dequant(rg[j], gcol + j));
+          const float u = bf16r(dequant(ru[j], gcol + 32 + j));
+          const float sg = bf16r(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+          v[j] = __fmul_rn(sg, u);
         }
-        continue;
-      }
-      for (int c = half; c < BN / 32; c += 2) {
-        uint32_t r[32];
-        tmem_ld32p(t_row + c * 32, r);
-        tmem_wait_fence<1>(r);
-        if (c + 2 >= BN / 32) release_acc(buf);  // this warp's last chunk
+        store_block(v, gcol / 2);
+      };
+      // Accumulator chunk c (output columns n0+32c .. +31) from its raw words.
+      auto plain_chunk = [&](const uint32_t* r, int c) {
         const int col0 = n0 + c * 32;
-        if (col0 >= args.n) continue;  // warp-uniform: the whole chunk is past the last column
-        if (args.out_mode == OUT_I32) {
+        if (col0 >= args.n) return;  // warp-uniform: the whole chunk is past the last column
+        if (EpiOf<EM>::out_mode == OUT_I32) {
           if (row_ok) {
             int32_t* out = static_cast<int32_t*>(args.y) + static_cast<int64_t>(row) * args.ldy + col0;
 #pragma unroll
@@ -568,15 +704,15 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
               *reinterpret_cast<uint4*>(out + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
             }
           }
-          continue;
+          return;
         }
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = dequant(r[j], col0 + j);
-        if (args.epilogue == H3B_EPI_GELU) {
+        if (EpiOf<EM>::epilogue == H3B_EPI_GELU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-        } else if (args.epilogue == H3B_EPI_GATE_RES && row_ok) {
+        } else if (EpiOf<EM>::epilogue == H3B_EPI_GATE_RES && row_ok) {
           const __nv_bfloat16* res = args.resid + static_cast<int64_t>(row) * args.ldy + col0;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -602,11 +738,54 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
           }
         }
         store_block(v, col0);
+      };
+      if constexpr (C::NVF4_PAIR) {
+        // Single accumulator: read this warp's four chunks (128 columns),
+        // release the accumulator to the next tile's MMAs, then compute.
+        const bool swi = EpiOf<EM>::epilogue == H3B_EPI_SWIGLU;
+        uint32_t racc[4][32];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = swi ? 2 * half + (i & 1) + 4 * (i >> 1) : half + 2 * i;
+          tmem_ld32p(t_row + c * 32, racc[i]);
+        }
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) reg_fence32(racc[i]);
+        release_acc(buf);
+        if (swi) {
+          swiglu_pair(racc[0], racc[1], half);
+          swiglu_pair(racc[2], racc[3], half + 2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) plain_chunk(racc[i], half + 2 * i);
+        }
+        continue;
+      }
+      if (EpiOf<EM>::epilogue == H3B_EPI_SWIGLU) {
+        for (int p = half; p < BN / 64; p += 2) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32p(t_row + p * 64, rg);
+          tmem_ld32p(t_row + p * 64 + 32, ru);
+          tc_wait_ld();
+          reg_fence32(rg);
+          reg_fence32(ru);
+          if (p + 2 >= BN / 64) release_acc(buf);  // this warp's last pair
+          swiglu_pair(rg, ru, p);
+        }
+        continue;
+      }
+      for (int c = half; c < BN / 32; c += 2) {
+        uint32_t r[32];
+        tmem_ld32p(t_row + c * 32, r);
+        tmem_wait_fence<1>(r);
+        if (c + 2 >= BN / 32) release_acc(buf);  // this warp's last chunk
+        plain_chunk(r, c);
       }
     }
     if (lane == 0) {
       bulk_wait_group<0>();  // stores complete before the CTA exits
-      if (args.out_mode == OUT_SEQ2HEAD) __threadfence_system();  // peer writes visible system-wide
+      if (EpiOf<EM>::out_mode == OUT_SEQ2HEAD) __threadfence_system();  // peer writes visible system-wide
     }
     __syncwarp();
     if (args.amax_out != nullptr) {
@@ -630,7 +809,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
   }
 }
 
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EM>
 int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                   cudaStream_t st, const PeerMaps* peer_maps) {
   using C = Cfg<KIND, PAIR>;
@@ -653,9 +832,16 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
   const size_t smem = smem_bytes<KIND, PAIR>();
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_kernel<KIND, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_kernel<KIND, PAIR, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return H3B_ERR_LAUNCH;
+    if constexpr (C::NVF4_PAIR) {
+      // setmaxnreg.inc waits for registers the launch must have provided:
+      // refuse to launch a build whose kernel got fewer than the split needs.
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, gemm_kernel<KIND, PAIR, EM>) != cudaSuccess || fa.numRegs < PAIR_LAUNCH_REGS)
+        return H3B_ERR_LAUNCH;
+    }
     attr_set = true;
   }
   const int m_tiles = static_cast<int>((args.m + BM * PAIR - 1) / (BM * PAIR));
@@ -678,23 +864,47 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, 2>, ta, tb, ty, pm, args) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, 2, EM>, ta, tb, ty, pm, args) != cudaSuccess)
       return H3B_ERR_LAUNCH;
   } else {
-    gemm_kernel<KIND, 1><<<units, C::THREADS, smem, st>>>(ta, tb, ty, pm, args);
+    gemm_kernel<KIND, 1, EM><<<units, C::THREADS, smem, st>>>(ta, tb, ty, pm, args);
   }
   return h3b::launch_status();
 }
 
 // CTA pairs for every GEMM with more than one 128-row tile of M; a single
 // row tile keeps one CTA per output tile (twice the CTAs for small M).
+template <int KIND, int EM>
+int launch_gemm_e(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
+                  cudaStream_t st, const PeerMaps* peer_maps) {
+  if (args.m > BM && !args.no_loads)
+    return launch_gemm_t<KIND, 2, EM>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  return launch_gemm_t<KIND, 1, EM>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+}
+
+// One kernel instance per epilogue mode (EpiMode): the output form first,
+// then the activation.
 template <int KIND>
 int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                 cudaStream_t st, const PeerMaps* peer_maps = nullptr) {
-  if constexpr (KIND == KIND_I8) {
-    if (args.m > BM) return launch_gemm_t<KIND, 2>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  if (args.out_mode == OUT_SEQ2HEAD)
+    return launch_gemm_e<KIND, EM_SEQ2HEAD>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  if (args.out_mode == OUT_I32) {
+    if constexpr (KIND == KIND_I8) return launch_gemm_e<KIND, EM_I32>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    return H3B_ERR_ARG;
   }
-  return launch_gemm_t<KIND, 1>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+  switch (args.epilogue) {
+    case H3B_EPI_STORE:
+      return launch_gemm_e<KIND, EM_STORE>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    case H3B_EPI_GELU:
+      return launch_gemm_e<KIND, EM_GELU>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    case H3B_EPI_GATE_RES:
+      return launch_gemm_e<KIND, EM_GATE_RES>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    case H3B_EPI_SWIGLU:
+      return launch_gemm_e<KIND, EM_SWIGLU>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    default:
+      return H3B_ERR_ARG;
+  }
 }
 
 // m == 0 (an empty batch) passes: the plain GEMM entries then return

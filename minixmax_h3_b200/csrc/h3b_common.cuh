@@ -289,6 +289,13 @@ H3B_DEV void cluster_sync() {
 H3B_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrive on the other CTA's mbarrier with the default semantics.  For a
+// hand-off of TMEM contents the arriving warp has completed
+// (tcgen05.wait::st / wait::ld, then tcgen05.fence::before_thread_sync),
+// which the cluster-scope release above would only delay (~1000 cycles).
+H3B_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // This CTA's share of a pair operand; the bytes complete on the leader's
 // mbarrier (`leader_bar`, a shared::cluster address).  No multicast.
 H3B_DEV void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t leader_bar) {
@@ -326,6 +333,17 @@ H3B_DEV void mma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Block-scaled NVFP4 pair MMA: each CTA's scale operands are read from its
+// own TMEM at the given columns.
+H3B_DEV void mma_nvf4_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa_tmem,
+                              uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
 }
 
 
