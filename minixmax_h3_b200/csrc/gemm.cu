@@ -642,6 +642,26 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         if (args.bias != nullptr) a = __fadd_rn(a, __bfloat162float(args.bias[col]));
         return a;
       };
+      // dequant of 32 consecutive columns with packed fp32x2 arithmetic (the
+      // same roundings as dequant, half the instructions).
+      auto dequant32 = [&](const uint32_t* r, int col0, float (&v)[32]) {
+        const float2 rs = make_float2(row_scale, row_scale);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float2 a;
+          if constexpr (KIND == KIND_I8) {
+            a = mul2(make_float2(static_cast<float>(static_cast<int32_t>(r[j])),
+                                 static_cast<float>(static_cast<int32_t>(r[j + 1]))), rs);
+            a = mul2(a, make_float2(__ldg(args.ws + col0 + j), __ldg(args.ws + col0 + j + 1)));
+          } else {
+            a = mul2(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), rs);
+          }
+          if (args.bias != nullptr)
+            a = add2(a, make_float2(__bfloat162float(args.bias[col0 + j]), __bfloat162float(args.bias[col0 + j + 1])));
+          v[j] = a.x;
+          v[j + 1] = a.y;
+        }
+      };
       // Stage a 32x32 bf16 block and TMA-store it at output column ocol.  A
       // staging buffer is reused every other block: first wait until at most
       // one store (the other buffer's) may still be reading shared memory.
@@ -707,8 +727,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
           return;
         }
         float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = dequant(r[j], col0 + j);
+        dequant32(r, col0, v);
         if (EpiOf<EM>::epilogue == H3B_EPI_GELU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);

@@ -501,6 +501,14 @@ H3B_DEV float2 add2(float2 a, float2 b) {
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return d;
 }
+// Two round-to-nearest products, bit-identical to two __fmul_rn.
+H3B_DEV float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
 
 // Three-input max (sm_100): halves the instruction count of row maxima.
 H3B_DEV float fmax3(float a, float b, float c) {
