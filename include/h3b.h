@@ -60,7 +60,8 @@ enum {
   H3B_EPI_STORE = 0,    /* y = acc*scales (+ bias)                            */
   H3B_EPI_GELU = 1,     /* y = gelu_erf(acc*scales (+ bias))                  */
   H3B_EPI_GATE_RES = 2, /* y[m,n] = resid[m,n] + (acc*scales (+bias)) * gate[n] */
-  H3B_EPI_SWIGLU = 3    /* y[m,j] = silu(g)*u of a row-interleaved fc1, see below */
+  H3B_EPI_SWIGLU = 3,   /* y[m,j] = silu(g)*u of a row-interleaved fc1, see below */
+  H3B_EPI_STORE_POSMAX = 4 /* as H3B_EPI_STORE; amax_out receives max(0, max y)  */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -119,7 +120,11 @@ H3B_API int h3b_quant_i8_rows_convrot(const void* x, int x_dtype, int64_t m, int
  * y[m,j] = bf16(bf16(silu(g)) * u) with g, u the bf16-rounded outputs of the
  * gate and up rows, the rounding chain of the reference's unfused
  * F.silu(gate) * up.  Needs n % 64 == 0.
- * amax_out (optional, caller-zeroed fp32) receives max |y| over the output.
+ * H3B_EPI_GELU: y = bf16(gelu(bf16(v))), the reference's F.gelu of the bf16
+ * linear output (model/dit.py:298-301 with the benchmark's GELU MLP).
+ * amax_out (optional, caller-zeroed fp32) receives max |y| over the output;
+ * under H3B_EPI_STORE_POSMAX it receives max(0, max y) instead (the input of
+ * h3b_gelu_amax_scan / h3b_quant_nvfp4_gelu).
  * k % 128 == 0, n % 32 == 0, ldy % 8 == 0.
  */
 H3B_API int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* w, const float* ws, const void* bias,
@@ -159,6 +164,34 @@ H3B_API int h3b_amax_bf16(const void* x, int64_t n, float* amax_out, h3b_stream_
  */
 H3B_API int h3b_quant_nvfp4(const void* x, int64_t m, int64_t k, int64_t ldx, const float* amax, uint8_t* codes,
                     uint8_t* sf, float* gs_out, int hi_first, h3b_stream_t stream);
+
+/*
+ * The MLP's activation fused with fc2's input quantisation (the fc1 ->
+ * gelu -> fc2 input of model/dit.py:120-129 / ops/fused_block.py:61-63 with
+ * the benchmark's GELU MLP): h3b_quant_nvfp4 of u = bf16(gelu(y)) computed on
+ * the fly from fc1's bf16 output y [m, k] (row stride ldy), u never written.
+ * The global scale needs max |u| before any code is written; it comes from
+ * ymax2 (fp32 [2], device):
+ *   ymax2[0] = max(0, max y)  (fc1 with H3B_EPI_STORE_POSMAX, max-reduced
+ *              across ranks when sharded),
+ *   ymax2[1] = max |u| by h3b_gelu_amax_scan (0 unless needed, see there),
+ * max |u| = a when a = bf16(gelu(ymax2[0])) >= 0.169921875 (GELU and bf16
+ * rounding are monotone for y >= 0, and |bf16(gelu(y))| <= 0.169921875 for
+ * y < 0), else ymax2[1].  Codes, scales and gs as h3b_quant_nvfp4.
+ * k % 64 == 0, ldy % 8 == 0, m >= 1.
+ */
+H3B_API int h3b_quant_nvfp4_gelu(const void* y, int64_t m, int64_t k, int64_t ldy, const float* ymax2,
+                                 uint8_t* codes, uint8_t* sf, float* gs_out, int hi_first, h3b_stream_t stream);
+
+/*
+ * ymax2[1] = max(ymax2[1], max |bf16(gelu(y))|) over y [m, k] (row stride
+ * ldy), computed only when bf16(gelu(ymax2[0])) < 0.169921875 (every block
+ * returns at once otherwise).  ymax2[1] must start at 0.  Run after fc1 and
+ * before the cross-rank max of ymax2: a rank whose own ymax2[0] is below the
+ * bound scans, and if the global one is too, every rank has scanned.
+ * k % 8 == 0, ldy % 8 == 0.
+ */
+H3B_API int h3b_gelu_amax_scan(const void* y, int64_t m, int64_t k, int64_t ldy, float* ymax2, h3b_stream_t stream);
 
 /*
  * Swap the two nibbles of every byte (checkpoint hi-first order <-> tensor-core

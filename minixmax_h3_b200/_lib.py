@@ -26,6 +26,8 @@ SIGNATURES: dict[str, list] = {
     "h3b_gemm_i8_acc_i32": [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_i64, c_ptr],
     "h3b_amax_bf16": [c_ptr, c_i64, c_ptr, c_ptr],
     "h3b_quant_nvfp4": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_ptr],
+    "h3b_quant_nvfp4_gelu": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_int, c_ptr],
+    "h3b_gelu_amax_scan": [c_ptr, c_i64, c_i64, c_i64, c_ptr, c_ptr],
     "h3b_nvfp4_swap_nibbles": [c_ptr, c_ptr, c_i64, c_ptr],
     "h3b_gemm_nvfp4_bf16": [c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64,
                             c_ptr, c_ptr, c_int, c_i64, c_i64, c_i64, c_ptr],

@@ -29,7 +29,7 @@ import torch.nn.functional as F
 from . import ops
 from .dist import is_distributed, state
 from .modules import Linear, Ops, QuantizedRows, QuantLinear, RMSNorm
-from .ops import EPI_GATE_RES, EPI_GELU, EPI_SWIGLU
+from .ops import EPI_GATE_RES, EPI_GELU, EPI_STORE_POSMAX, EPI_SWIGLU
 from .timing import TIMER
 from .ulysses import (all_gather_kv, all_to_all_heads, all_to_all_qkv, check_scheme, clip_mod_segments,
                       peer_buffer, phase_barrier, ring_attention, split_range)
@@ -239,9 +239,11 @@ class Attention(nn.Module):
 
 class MLP(nn.Module):
     """fc1 -> activation -> fc2 (model/dit.py:291-301).  act="swiglu" is the
-    reference MLP (fc1: hidden -> 2*ffn, silu(gate)*up); act="gelu" is the
-    benchmark's 4x GELU MLP (fc1: hidden -> ffn, exact-erf GELU fused into the
-    fc1 epilogue)."""
+    reference MLP (fc1: hidden -> 2*ffn, silu(gate)*up, fused into fc1's
+    epilogue); act="gelu" is the benchmark's 4x GELU MLP (fc1: hidden -> ffn,
+    exact-erf GELU of fc1's bf16 output applied inside fc2's NVFP4 input
+    quantiser; fused into fc1's epilogue when fc2 is INT8 or has a
+    pre_quant_scale)."""
 
     def __init__(self, hidden, ffn, dtype=None, device=None, operations=None, act: str = "swiglu"):
         super().__init__()
@@ -256,6 +258,20 @@ class MLP(nn.Module):
     def forward(self, h: torch.Tensor, *, amax_h=None, resid=None, gate=None, row_sel=None) -> torch.Tensor:
         amax_u = torch.zeros(1, dtype=torch.float32, device=h.device)
         amax_h = global_amax_(amax_h, self.fc1)
+        if self.act == "gelu" and self.fc2.quant_format == "nvfp4" and self.fc2.pre_quant_scale is None:
+            # fc1 stores its bf16 output y and max(0, max y); GELU runs inside
+            # fc2's NVFP4 input quantiser, u = bf16(gelu(y)) as the reference's
+            # F.gelu of the bf16 linear output.  max |u| follows from max y
+            # (a scan covers the case the bound does not settle).
+            ymax2 = torch.zeros(2, dtype=torch.float32, device=h.device)
+            y = self.fc1.forward_fused(h, amax=amax_h, epilogue=EPI_STORE_POSMAX, amax_out=ymax2[:1])
+            with TIMER.span("quant"):
+                ops.gelu_amax_scan(y, ymax2)
+            global_amax_(ymax2, self.fc2)
+            if resid is not None:
+                return self.fc2.forward_gelu_input(y, ymax2, epilogue=EPI_GATE_RES, resid=resid, gate=gate,
+                                                   row_sel=row_sel)
+            return self.fc2.forward_gelu_input(y, ymax2)
         if self.act == "gelu":
             u = self.fc1.forward_fused(h, amax=amax_h, epilogue=EPI_GELU, amax_out=amax_u)
         else:

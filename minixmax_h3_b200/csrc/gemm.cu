@@ -118,6 +118,7 @@ struct GemmArgs {
   int heads_per_rank;  // OUT_SEQ2HEAD: H / world_size
   int hd;              // OUT_SEQ2HEAD: H * 128 (columns per q|k|v part)
   int no_loads;        // wait self-test: the producer issues nothing (h3b_selftest_wait_timeout)
+  int amax_signed;     // amax_out receives max(0, max y) instead of max |y| (H3B_EPI_STORE_POSMAX)
 };
 
 // PAIR = 1: one CTA per 128 x BN tile.  PAIR = 2: a cluster of two CTAs per
@@ -210,8 +211,6 @@ constexpr size_t smem_bytes() {
 static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
                   smem_bytes<KIND_I8, 1>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 2>() <= 227 * 1024,
               "shared memory budget");
-
-H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
 // Lane 0 waits, the verdict is broadcast so the whole warp stays converged.
 template <bool SPIN = false>
@@ -677,9 +676,14 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
           *reinterpret_cast<uint4*>(sb + swz64(lane, q4)) = pk;
           if (args.amax_out != nullptr && row_ok) {
             const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+            if (args.amax_signed) {  // max of the stored values, floored at 0 by y_amax's start
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
+              for (int e = 0; e < 4; ++e) y_amax = fmax3(y_amax, bf16lo_to_f32(w4[e]), bf16hi_to_f32(w4[e]));
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                y_amax = fmaxf(y_amax, fmaxf(fabsf(bf16lo_to_f32(w4[e])), fabsf(bf16hi_to_f32(w4[e]))));
+            }
           }
         }
         fence_proxy_async_smem();
@@ -730,7 +734,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         dequant32(r, col0, v);
         if (EpiOf<EM>::epilogue == H3B_EPI_GELU) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(bf16r(v[j]));  // gelu of the bf16 linear output
         } else if (EpiOf<EM>::epilogue == H3B_EPI_GATE_RES && row_ok) {
           const __nv_bfloat16* res = args.resid + static_cast<int64_t>(row) * args.ldy + col0;
 #pragma unroll
@@ -921,6 +925,12 @@ int launch_gemm(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row
       return launch_gemm_e<KIND, EM_GATE_RES>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
     case H3B_EPI_SWIGLU:
       return launch_gemm_e<KIND, EM_SWIGLU>(a, b, a_row_bytes, b_row_bytes, args, st, peer_maps);
+    case H3B_EPI_STORE_POSMAX: {
+      GemmArgs s = args;
+      s.epilogue = H3B_EPI_STORE;
+      s.amax_signed = 1;
+      return launch_gemm_e<KIND, EM_STORE>(a, b, a_row_bytes, b_row_bytes, s, st, peer_maps);
+    }
     default:
       return H3B_ERR_ARG;
   }
@@ -944,7 +954,7 @@ extern "C" int h3b_gemm_i8_bf16(const int8_t* q, const float* xs, const int8_t* 
   if (q == nullptr || xs == nullptr || w == nullptr || ws == nullptr || y == nullptr) return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 128);
   if (rc != H3B_OK) return rc;
-  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_SWIGLU) return H3B_ERR_ARG;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_STORE_POSMAX) return H3B_ERR_ARG;
   if (epilogue == H3B_EPI_SWIGLU && (n % 64) != 0) return H3B_ERR_SHAPE;
   if (ldy < (epilogue == H3B_EPI_SWIGLU ? n / 2 : n) || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;
@@ -998,7 +1008,7 @@ extern "C" int h3b_gemm_nvfp4_bf16(const uint8_t* a_codes, const uint8_t* a_sf, 
     return H3B_ERR_ARG;
   int rc = check_common(m, n, k, 256);
   if (rc != H3B_OK) return rc;
-  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_SWIGLU) return H3B_ERR_ARG;
+  if (epilogue < H3B_EPI_STORE || epilogue > H3B_EPI_STORE_POSMAX) return H3B_ERR_ARG;
   if (epilogue == H3B_EPI_SWIGLU && (n % 64) != 0) return H3B_ERR_SHAPE;
   if (ldy < (epilogue == H3B_EPI_SWIGLU ? n / 2 : n) || (ldy % 8) != 0) return H3B_ERR_SHAPE;
   if (epilogue == H3B_EPI_GATE_RES && (resid == nullptr || gate == nullptr || gate_ld < 0)) return H3B_ERR_ARG;

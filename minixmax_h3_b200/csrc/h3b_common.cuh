@@ -471,6 +471,22 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t m, uint32_t n) {
 // ----------------------------------------------------------------------------
 // fp32 -> nearest-even bf16 -> fp32 (one rounding step of a bf16 computation).
 H3B_DEV float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Exact-erf GELU in fp32 (torch.nn.functional.gelu, approximate="none").
+H3B_DEV float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+// max |bf16(gelu(y))| over y < 0 is bf16(gelu(-0.7518..)) = -0.169921875 in
+// magnitude: GELU's minimum is -0.16997, which rounds to 174 * 2^-10.
+constexpr float GELU_BF16_NEG_BOUND = 0.169921875f;
+
+// Global max |u| of u = bf16(gelu(y)) over bf16 values y, from
+//   ymax2[0] = max(0, max y)   (GELU and bf16 rounding are monotone on y >= 0)
+//   ymax2[1] = max |bf16(gelu(y))| by a full scan, needed (and present) only
+//              when bf16(gelu(ymax2[0])) is below the bound for y < 0.
+H3B_DEV float gelu_input_amax(const float* ymax2) {
+  const float a = bf16r(gelu_erf(ymax2[0]));
+  return a >= GELU_BF16_NEG_BOUND ? a : ymax2[1];
+}
 // The same rounding for two values with one packed conversion.
 H3B_DEV float2 bf16r2(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);

@@ -336,6 +336,9 @@ H3B_DEV uint32_t e2m1x8(const float* r, int hi_first) {
   return out;
 }
 
+// GELU: the input is fc1's bf16 output y and the quantised value is
+// u = bf16(gelu(y)) (h3b_quant_nvfp4_gelu); amax_ptr then points at ymax2.
+template <bool GELU>
 __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int64_t m,
                                                           int64_t k, int64_t ldx, int64_t rows_padded,
                                                           const float* __restrict__ amax_ptr,
@@ -346,7 +349,7 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
   if (item >= rows_padded * groups) return;
   const int64_t row = item / groups;
   const int64_t g = item - row * groups;
-  const float gs = nvfp4_global_scale(*amax_ptr);
+  const float gs = nvfp4_global_scale(GELU ? gelu_input_amax(amax_ptr) : *amax_ptr);
   if (item == 0) *gs_out = gs;
   // blocked layout: ((r/128)*ncb + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4, ncb = groups
   const int64_t sf_off = ((row >> 7) * groups + g) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4;
@@ -373,6 +376,10 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
       for (int j = 0; j < 8; ++j) {
         f[j] = a0[j];
         f[8 + j] = a1[j];
+      }
+      if constexpr (GELU) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] = bf16r(gelu_erf(f[j]));
       }
     }
     float amax_b = 0.0f;
@@ -568,9 +575,61 @@ extern "C" int h3b_quant_nvfp4(const void* x, int64_t m, int64_t k, int64_t ldx,
   const int64_t blocks = (items + 255) / 256;
   if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  quant_nvfp4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), m, k,
-                                                                     ldx, rows_padded, amax, codes, sf, gs_out,
-                                                                     hi_first);
+  quant_nvfp4_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), m, k, ldx, rows_padded, amax, codes, sf, gs_out, hi_first);
+  return h3b::launch_status();
+}
+
+extern "C" int h3b_quant_nvfp4_gelu(const void* y, int64_t m, int64_t k, int64_t ldy, const float* ymax2,
+                                    uint8_t* codes, uint8_t* sf, float* gs_out, int hi_first, h3b_stream_t stream) {
+  if (y == nullptr || ymax2 == nullptr || codes == nullptr || sf == nullptr || gs_out == nullptr)
+    return H3B_ERR_ARG;
+  if (m <= 0 || k <= 0 || (k % 64) != 0 || ldy < k || (ldy % 8) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(y) || !h3b::aligned16(codes) || (reinterpret_cast<uintptr_t>(sf) & 3u) != 0)
+    return H3B_ERR_ALIGN;
+  const int64_t rows_padded = (m + 127) / 128 * 128;
+  const int64_t items = rows_padded * (k / 64);
+  const int64_t blocks = (items + 255) / 256;
+  if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  quant_nvfp4_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(y), m, k, ldy, rows_padded, ymax2, codes, sf, gs_out, hi_first);
+  return h3b::launch_status();
+}
+
+// ymax2[1] = max |bf16(gelu(y))| when bf16(gelu(ymax2[0])) is below the
+// bound for negative inputs (every block leaves at once otherwise).  Rows of
+// k bf16 values with row stride ldy, 8 values per step.
+__global__ void __launch_bounds__(256) gelu_amax_scan_kernel(const __nv_bfloat16* __restrict__ y, int64_t m,
+                                                             int64_t k, int64_t ldy, float* __restrict__ ymax2) {
+  __shared__ float red[33];
+  if (bf16r(gelu_erf(ymax2[0])) >= GELU_BF16_NEG_BOUND) return;  // uniform across the grid
+  const int64_t vpr = k >> 3;  // 8-value vectors per row
+  const int64_t nvec = m * vpr;
+  float amax = 0.0f;
+  for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += static_cast<int64_t>(gridDim.x) * 256) {
+    const int64_t row = i / vpr;
+    const uint4 v = ld_nc_v4(y + row * ldy + (i - row * vpr) * 8);
+    float f[8];
+    unpack8<__nv_bfloat16>(v, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(bf16r(gelu_erf(f[j]))));
+  }
+  amax = block_max<256>(amax, red);
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned int*>(ymax2 + 1), __float_as_uint(amax));
+}
+
+extern "C" int h3b_gelu_amax_scan(const void* y, int64_t m, int64_t k, int64_t ldy, float* ymax2,
+                                  h3b_stream_t stream) {
+  if (y == nullptr || ymax2 == nullptr) return H3B_ERR_ARG;
+  if (m < 0 || k <= 0 || (k % 8) != 0 || ldy < k || (ldy % 8) != 0) return H3B_ERR_SHAPE;
+  if (!h3b::aligned16(y)) return H3B_ERR_ALIGN;
+  if (m == 0) return H3B_OK;
+  const int64_t nvec = m * (k / 8);
+  const int64_t want = (nvec + 255) / 256;
+  const int blocks = static_cast<int>(want < 4 * h3b::num_sms() ? want : 4 * h3b::num_sms());
+  gelu_amax_scan_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), m, k, ldy, ymax2);
   return h3b::launch_status();
 }
 

@@ -241,6 +241,25 @@ class QuantLinear(nn.Module):
         return self._run(x, amax=amax, epilogue=epilogue, resid=resid, gate=gate, row_sel=row_sel,
                          amax_out=amax_out, out=out)
 
+    def forward_gelu_input(self, y: torch.Tensor, ymax2: torch.Tensor, *, epilogue: int = EPI_STORE,
+                           resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+                           row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,
+                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """fc2 of the GELU MLP fed fc1's bf16 pre-activation y: the GELU is
+        applied inside this layer's NVFP4 input quantiser
+        (ops.quant_nvfp4_gelu), so activation and quantisation are one pass
+        over y and u = bf16(gelu(y)) is never written.  ymax2: fp32 [2] from
+        fc1's EPI_STORE_POSMAX max and ops.gelu_amax_scan (max-reduced across
+        ranks).  NVFP4 layers without a pre_quant_scale only."""
+        if self.quant_format != "nvfp4" or self.pre_quant_scale is not None:
+            raise ValueError("forward_gelu_input needs an NVFP4 layer without a pre_quant_scale")
+        self.prepare_cube()
+        with TIMER.span("quant"):
+            a = ops.quant_nvfp4_gelu(y, ymax2)
+        with TIMER.span("gemm", *self._gemm_cost(a.rows)):
+            return ops.gemm_nvfp4(a, self._w_nvfp4, self._bias(y), epilogue=epilogue, resid=resid, gate=gate,
+                                  row_sel=row_sel, amax_out=amax_out, out=out)
+
     def _run(self, x, *, amax: Optional[torch.Tensor] = None, epilogue: int = EPI_STORE,
              resid: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
              row_sel: Optional[torch.Tensor] = None, amax_out: Optional[torch.Tensor] = None,

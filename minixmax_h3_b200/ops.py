@@ -14,7 +14,7 @@ import torch
 
 from ._lib import call
 
-EPI_STORE, EPI_GELU, EPI_GATE_RES, EPI_SWIGLU = 0, 1, 2, 3
+EPI_STORE, EPI_GELU, EPI_GATE_RES, EPI_SWIGLU, EPI_STORE_POSMAX = 0, 1, 2, 3, 4
 
 
 def _stream(t: torch.Tensor) -> int:
@@ -175,6 +175,41 @@ def quant_nvfp4(x: torch.Tensor, *, hi_first: bool = False,
     gs = torch.empty((1,), dtype=torch.float32, device=x.device)
     call("h3b_quant_nvfp4", x2.data_ptr(), m, k, ld, amax_t.data_ptr(), codes.data_ptr(), sf.data_ptr(),
          gs.data_ptr(), 1 if hi_first else 0, _stream(x))
+    return NVFP4Tensor(codes, sf, gs, m, k, hi_first)
+
+
+def gelu_amax_scan(y: torch.Tensor, ymax2: torch.Tensor) -> torch.Tensor:
+    """ymax2[1] = max |bf16(gelu(y))| over fc1's bf16 output y when the bound
+    from ymax2[0] = max(0, max y) does not settle max |u| (h3b_gelu_amax_scan);
+    ymax2 is an fp32 [2] device tensor, ymax2[1] zero on entry."""
+    _cuda(y, ymax2)
+    if y.dtype != torch.bfloat16:
+        raise TypeError("gelu_amax_scan expects bf16 input")
+    if ymax2.dtype != torch.float32 or ymax2.numel() != 2 or not ymax2.is_contiguous():
+        raise ValueError("ymax2 must be a contiguous fp32 tensor of 2 elements")
+    y2, m, k, ld = _rows(y)
+    call("h3b_gelu_amax_scan", y2.data_ptr(), m, k, ld, ymax2.data_ptr(), _stream(y))
+    return ymax2
+
+
+def quant_nvfp4_gelu(y: torch.Tensor, ymax2: torch.Tensor, *, hi_first: bool = False) -> NVFP4Tensor:
+    """NVFP4 quantisation of u = bf16(gelu(y)) computed from fc1's bf16 output
+    y on the fly (h3b_quant_nvfp4_gelu): the MLP activation fused with fc2's
+    input quantisation.  ymax2: fp32 [2] from the fc1 GEMM's
+    EPI_STORE_POSMAX max and gelu_amax_scan, max-reduced across ranks."""
+    _cuda(y, ymax2)
+    if y.dtype != torch.bfloat16:
+        raise TypeError("quant_nvfp4_gelu expects bf16 input")
+    if ymax2.dtype != torch.float32 or ymax2.numel() != 2 or not ymax2.is_contiguous():
+        raise ValueError("ymax2 must be a contiguous fp32 tensor of 2 elements")
+    y2, m, k, ld = _rows(y)
+    if m == 0:
+        raise ValueError("quant_nvfp4_gelu needs at least one row")
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device=y.device)
+    sf = torch.empty((sf_blocked_bytes(m, k),), dtype=torch.uint8, device=y.device)
+    gs = torch.empty((1,), dtype=torch.float32, device=y.device)
+    call("h3b_quant_nvfp4_gelu", y2.data_ptr(), m, k, ld, ymax2.data_ptr(), codes.data_ptr(), sf.data_ptr(),
+         gs.data_ptr(), 1 if hi_first else 0, _stream(y))
     return NVFP4Tensor(codes, sf, gs, m, k, hi_first)
 
 

@@ -16,8 +16,11 @@ that stage: the norm + modulate rows, the activation codes and block scales
 (bit-exact, with the whole tensor's global scale), the QKV GEMM rows, the
 q/k RMSNorm + RoPE rows, the attention rows of two heads (including the last
 rows and the partial last K/V tile: 498,272 mod 128 = 96) against all keys,
-the out-projection with its gate-residual epilogue, fc1 with GELU and fc2
-with its gate-residual epilogue.  Bars: bit-exact for codes, scales and
+the out-projection with its gate-residual epilogue, fc1 (bf16 output and
+its max), the GELU applied inside fc2's input quantiser (codes and scales
+bit-exact against the oracle's quantisation of F.gelu of fc1's output, with
+max |u| from max y checked against the full maximum) and fc2 with its
+gate-residual epilogue.  Bars: bit-exact for codes, scales and
 accumulators; helpers.assert_close_bf16 (scaled max-abs <= 2e-2, cosine >=
 0.9995) for bf16 outputs, 1e-2 for the norm and RoPE rows as in their own
 tests.
@@ -27,6 +30,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 from helpers import assert_close_bf16
 from oracle import h3_oracle as O
@@ -141,7 +145,7 @@ def _w_dict(ql) -> dict:
 def test_cfg5_block_sampled_stages(cuda):
     from minixmax_h3_b200 import ops
     from minixmax_h3_b200.block import RopeSpec, init_block_random, timestep_embedding
-    from minixmax_h3_b200.ops import EPI_GATE_RES, EPI_GELU
+    from minixmax_h3_b200.ops import EPI_GATE_RES, EPI_STORE_POSMAX
 
     hidden, heads, n_text, grid = 3072, 24, 512, (61, 68, 120)
     ffn = 4 * hidden
@@ -221,25 +225,37 @@ def test_cfg5_block_sampled_stages(cuda):
     y_ref = O.nvfp4_linear_w4a4(ao_rows, _w_dict(qo), hidden).to(torch.bfloat16)
     assert_close_bf16(_take(x, rows), O.mod_gate(x_before.clone(), cpu["gate1"], y_ref, segs))
 
-    # norm2 + modulate, fc1 with GELU (+ |u| max)
+    # norm2 + modulate, fc1 storing its bf16 output y and max(0, max y)
     amax_h2 = torch.zeros(1, dtype=torch.float32, device=cuda)
     h2 = ops.rmsnorm_modulate(x, blk.norm2.weight, shift2, scale2, 1e-6, row_sel=sel, amax_out=amax_h2)
     f1 = blk.mlp.fc1
     f1.prepare_cube()
     a2 = ops.quant_nvfp4(h2, amax_t=amax_h2)
     a2_rows = _check_quant(a2, h2, rows, hidden, amax_h2)
-    amax_u = torch.zeros(1, dtype=torch.float32, device=cuda)
-    u = ops.gemm_nvfp4(a2, f1._w_nvfp4, epilogue=EPI_GELU, amax_out=amax_u)
-    u_ref = torch.nn.functional.gelu(O.nvfp4_linear_w4a4(a2_rows, _w_dict(f1), hidden).to(torch.bfloat16).float())
-    assert_close_bf16(_take(u, rows), u_ref)
-    assert amax_u.item() == u.abs().max().float().item()
+    ymax2 = torch.zeros(2, dtype=torch.float32, device=cuda)
+    y = ops.gemm_nvfp4(a2, f1._w_nvfp4, epilogue=EPI_STORE_POSMAX, amax_out=ymax2[:1])
+    y_ref = O.nvfp4_linear_w4a4(a2_rows, _w_dict(f1), hidden).to(torch.bfloat16)
+    assert_close_bf16(_take(y, rows), y_ref)
+    assert ymax2[0].item() == max(0.0, y.max().float().item())
+
+    # GELU inside fc2's input quantiser: u = bf16(gelu(y)) (torch's F.gelu of
+    # the bf16 output on the GPU is the same chain); max |u| from max y
+    ops.gelu_amax_scan(y, ymax2)
+    assert ymax2[1].item() == 0.0  # the bound settles max |u| at this scale
+    amax_u = F.gelu(ymax2[:1].to(torch.bfloat16)).float()
+    chunk = 1 << 16
+    assert max(F.gelu(y[i:i + chunk]).abs().max().float().item() for i in range(0, s_len, chunk)) == amax_u.item()
+    au = ops.quant_nvfp4_gelu(y, ymax2)
+    au_rows = _nvfp4_rows(au, rows, ffn)
+    want = O.nvfp4_quantize(F.gelu(y[rows.to(cuda)]).cpu(), hi_first=True, amax=amax_u.item())
+    assert torch.equal(au_rows["gs"], want["gs"])
+    assert torch.equal(au_rows["codes"], want["codes"])
+    assert torch.equal(au_rows["sf_logical"], want["sf_logical"])
 
     # fc2 with the gate-residual epilogue
     x_before = _take(x, rows)
     f2 = blk.mlp.fc2
     f2.prepare_cube()
-    au = ops.quant_nvfp4(u, amax_t=amax_u)
-    au_rows = _check_quant(au, u, rows, ffn, amax_u)
     ops.gemm_nvfp4(au, f2._w_nvfp4, epilogue=EPI_GATE_RES, resid=x, gate=gate2, row_sel=sel)
     y2 = O.nvfp4_linear_w4a4(au_rows, _w_dict(f2), ffn).to(torch.bfloat16)
     assert_close_bf16(_take(x, rows), O.mod_gate(x_before.clone(), cpu["gate2"], y2, segs))
