@@ -12,7 +12,10 @@ import sys
 from types import SimpleNamespace
 from typing import Optional
 
-REF_ROOT = os.environ.get("H3B_REFERENCE_ROOT", "/root/reference")
+# The reference checkout sits beside this repository (``../reference``);
+# H3B_REFERENCE_ROOT overrides the location.
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_ROOT = os.environ.get("H3B_REFERENCE_ROOT", os.path.join(os.path.dirname(_REPO), "reference"))
 REF_SRC = os.path.join(REF_ROOT, "Ref2VA-910C-FastAPI-INT8-CANN9.1.0", "runtime", "src")
 
 
