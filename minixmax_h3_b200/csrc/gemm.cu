@@ -147,6 +147,7 @@ struct Cfg {
   static constexpr int SF_BASE = NACC * BN;    // NVFP4 scale slots follow the accumulators
   static constexpr int SF_SLOTS = NVF4_PAIR ? 5 : 2;  // NVFP4 scale slots in TMEM, one K slab each
   static constexpr int SF_WPQ = NVF4_PAIR ? 1 : 2;    // NVFP4 scale writer warps per TMEM lane quadrant
+  static constexpr int OUT_BUFS = 2;                   // epilogue staging buffers per warp (32x32 bf16 each)
   static constexpr int TMEM_COLS = 512;
   static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
@@ -206,7 +207,7 @@ struct __align__(8) Barriers {
 template <int KIND, int PAIR>
 constexpr size_t smem_bytes() {
   return 1024 /*alignment slack*/ + static_cast<size_t>(Cfg<KIND, PAIR>::STAGES) * Cfg<KIND, PAIR>::STAGE_BYTES +
-         EPI_WARPS * 2 * OUT_STAGE_BYTES + sizeof(Barriers);
+         EPI_WARPS * Cfg<KIND, PAIR>::OUT_BUFS * OUT_STAGE_BYTES + sizeof(Barriers);
 }
 static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
                   smem_bytes<KIND_I8, 1>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 2>() <= 227 * 1024,
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
   uint8_t* sSFA = sB + STAGES * C::B_BYTES;             // used by KIND_NVF4 only
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
   uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;       // 4 warps x 2 staging buffers, 1024-aligned
-  Barriers* bars = reinterpret_cast<Barriers*>(sOut + EPI_WARPS * 2 * OUT_STAGE_BYTES);
+  Barriers* bars = reinterpret_cast<Barriers*>(sOut + EPI_WARPS * C::OUT_BUFS * OUT_STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -585,10 +586,10 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
     const int half = (warp - C::EPI_WARP0) / 4;  // the quadrant's two warps take alternate 32-column chunks
-    uint8_t* out_stage = sOut + (warp - C::EPI_WARP0) * 2 * OUT_STAGE_BYTES;
+    uint8_t* out_stage = sOut + (warp - C::EPI_WARP0) * C::OUT_BUFS * OUT_STAGE_BYTES;
     float y_amax = 0.0f;                    // max |y| over every tile this thread stored
     int local = 0;
-    int stage_seq = 0;                      // alternates this warp's two staging buffers
+    int stage_seq = 0;                      // cycles through this warp's staging buffers
     // acc_empty lives in the leader; the peer's warps arrive remotely.
     auto release_acc = [&](int buf) {
       tc_fence_before();
@@ -662,11 +663,12 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         }
       };
       // Stage a 32x32 bf16 block and TMA-store it at output column ocol.  A
-      // staging buffer is reused every other block: first wait until at most
-      // one store (the other buffer's) may still be reading shared memory.
+      // staging buffer is reused every OUT_BUFS blocks: first wait until at
+      // most OUT_BUFS-1 stores (the other buffers') may still be reading
+      // shared memory.
       auto store_block = [&](const float (&v)[32], int ocol) {
-        uint8_t* sb = out_stage + (stage_seq & 1) * OUT_STAGE_BYTES;
-        if (lane == 0) bulk_wait_group_read<1>();
+        uint8_t* sb = out_stage + (stage_seq % C::OUT_BUFS) * OUT_STAGE_BYTES;
+        if (lane == 0) bulk_wait_group_read<C::OUT_BUFS - 1>();
         __syncwarp();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
