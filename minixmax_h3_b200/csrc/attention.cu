@@ -100,6 +100,7 @@ struct AttnArgs {
   __nv_bfloat16* o;
   __nv_bfloat16* o_peers[MAX_PEERS];  // head->seq scatter destinations (peer_mode)
   int peer_mode;
+  int o_wide;  // every destination and both strides 32-byte aligned: 32-byte row stores
   int s_local;
   int head0;
   float* lse;
@@ -510,7 +511,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32p(o_tmem + c * 32, r);
         tmem_wait_fence<1>(r);
-        if (q_row < args.s_q) {
+        if (q_row < args.s_q && args.o_wide) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              w[t] = pack_bf16x2(__uint_as_float(r[e + 2 * t]) * inv_l, __uint_as_float(r[e + 2 * t + 1]) * inv_l);
+              o_amax = fmaxf(o_amax, fmaxf(fabsf(bf16lo_to_f32(w[t])), fabsf(bf16hi_to_f32(w[t]))));
+            }
+            st_global_v8(orow + c * 32 + e, w);
+          }
+        } else if (q_row < args.s_q) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             uint4 v;
@@ -588,6 +600,15 @@ int launch_attention(const void* q, const void* k, const void* v, AttnArgs a, in
   return h3b::launch_status();
 }
 
+// 32-byte output stores need every destination base 32-byte aligned and both
+// strides (elements) multiples of 16; row offsets within a head are 32-value
+// chunks, so every store address is then 32-byte aligned.
+int wide_rows_ok(void* const* bufs, int64_t n, int64_t seq_stride, int64_t head_stride) {
+  for (int64_t r = 0; r < n; ++r)
+    if ((reinterpret_cast<uintptr_t>(bufs[r]) & 31u) != 0) return 0;
+  return (seq_stride % 16 == 0 && head_stride % 16 == 0) ? 1 : 0;
+}
+
 }  // namespace
 
 extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, float* amax_out,
@@ -603,6 +624,7 @@ extern "C" int h3b_attention_fwd(const void* q, const void* k, const void* v, vo
   a.amax_out = amax_out;
   a.o_seq_stride = o_seq_stride;
   a.o_head_stride = o_head_stride;
+  a.o_wide = wide_rows_ok(&o, 1, o_seq_stride, o_head_stride);
   return launch_attention(q, k, v, a, heads, s_q, s_kv, q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride,
                           scale, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -629,6 +651,7 @@ extern "C" int h3b_attention_fwd_head2seq(const void* q, const void* k, const vo
   a.amax_out = amax_out;
   a.o_seq_stride = o_seq_stride;
   a.o_head_stride = o_head_stride;
+  a.o_wide = wide_rows_ok(o_bufs, world_size, o_seq_stride, o_head_stride);
   return launch_attention(q, k, v, a, heads, s_q, s_kv, q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride,
                           scale, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -501,6 +501,15 @@ H3B_DEV uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// One 32-byte global store (sm_100 256-bit vector store).  The address must
+// be 32-byte aligned.  Over NVLink a 32-byte granule written whole costs its
+// own bytes; a 16-byte store costs a full granule.
+H3B_DEV void st_global_v8(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Packed fp32x2 arithmetic (sm_100): two lanes of work per instruction.
 H3B_DEV float2 fma2(float2 a, float2 b, float2 c) {
   float2 d;

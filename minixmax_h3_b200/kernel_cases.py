@@ -11,6 +11,7 @@
     python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate --m 131072 --k 3072
     python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate_quant_i8 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases rmsnorm_modulate_quant_i8_convrot --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases exchange_2gpu --m 8192 --heads 24 --k 3072   # needs 2 GPUs
 
 Each case allocates its inputs once, launches the kernel `--warmup` times,
 then `--iters` times between CUDA events on the launching stream, and prints
@@ -67,11 +68,55 @@ def _gemm(case: str, m: int, n: int, k: int, warmup: int, iters: int, g, dev, ep
     return {"m": m, "n": n, "k": k, "epilogue": epi, "ms": ms, "tflops": flops / ms / 1e9, "flops": flops}
 
 
+def _exchange_2gpu(s_local: int, heads: int, hidden: int, warmup: int, iters: int, g, dev) -> None:
+    """Rank 0 of a 2-rank Ulysses group, both GPUs driven by this one process:
+    the QKV GEMM with the seq->head scatter fused into its epilogue and the
+    attention with the head->seq scatter, each against the same kernel
+    writing locally.  Half of each fused output crosses NVLink (peer access
+    enabled between the two devices; no kernel waits on the other GPU)."""
+    from cuda.bindings import runtime as rt
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("exchange_2gpu needs 2 GPUs")
+    peer = torch.device("cuda", 1)
+    torch.cuda.set_device(dev)
+    (err,) = rt.cudaDeviceEnablePeerAccess(1, 0)
+    if err not in (rt.cudaError_t.cudaSuccess, rt.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+        raise SystemExit(f"cudaDeviceEnablePeerAccess: {err}")
+    hl, s = heads // 2, 2 * s_local
+    # QKV projection of this rank's s_local tokens
+    x = torch.randn(s_local, hidden, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(3 * heads * 128, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    xa, wq = ops.quant_nvfp4(x), ops.quant_nvfp4(w)
+    recv = [torch.zeros(s, 3, hl, 128, dtype=torch.bfloat16, device=d) for d in (dev, peer)]
+    y = torch.empty(s_local, 3 * heads * 128, dtype=torch.bfloat16, device=dev)
+    flops = 2.0 * s_local * w.shape[0] * hidden
+    ms_plain = _time(lambda: ops.gemm_nvfp4(xa, wq, out=y), warmup, iters)
+    ms_fused = _time(lambda: ops.gemm_nvfp4_seq2head(xa, wq, None, [r.data_ptr() for r in recv], 0, heads),
+                     warmup, iters)
+    peer_bytes = s_local * 3 * hl * 128 * 2
+    print(json.dumps({"case": "gemm_nvfp4_seq2head", "m": s_local, "n": w.shape[0], "k": hidden,
+                      "ms_plain": ms_plain, "ms_fused": ms_fused, "tflops_fused": flops / ms_fused / 1e9,
+                      "peer_bytes": peer_bytes, "peer_gbs": peer_bytes / ms_fused / 1e6}), flush=True)
+    # attention over this rank's heads of all s tokens, rows scattered to the token owners
+    q, k, v = (torch.randn(s, hl, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    o_plain = torch.empty(s, hl, 128, dtype=torch.bfloat16, device=dev)
+    outs = [torch.zeros(s_local, heads, 128, dtype=torch.bfloat16, device=d) for d in (dev, peer)]
+    aflops = 4.0 * s * s * 128 * hl
+    ms_plain = _time(lambda: ops.attention(q, k, v, out=o_plain), warmup, iters)
+    ms_fused = _time(lambda: ops.attention_head2seq(q, k, v, [o.data_ptr() for o in outs], s_local=s_local, head0=0,
+                                                    total_heads=heads), warmup, iters)
+    peer_bytes = s_local * hl * 128 * 2
+    print(json.dumps({"case": "attention_head2seq", "seq": s, "heads": hl, "ms_plain": ms_plain,
+                      "ms_fused": ms_fused, "tflops_fused": aflops / ms_fused / 1e9, "peer_bytes": peer_bytes,
+                      "peer_gbs": peer_bytes / ms_fused / 1e6}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("case", choices=["attention", "gemm_nvfp4", "gemm_i8", "quant_nvfp4", "quant_i8",
                                        "quant_i8_convrot", "qk_rope", "rmsnorm_modulate", "rmsnorm_modulate_quant_i8",
-                                       "rmsnorm_modulate_quant_i8_convrot", "gemm_sweep"])
+                                       "rmsnorm_modulate_quant_i8_convrot", "gemm_sweep", "exchange_2gpu"])
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--heads", type=int, default=24)
     ap.add_argument("--m", type=int, default=8192)
@@ -104,6 +149,9 @@ def main() -> None:
         for case in ("gemm_i8", "gemm_nvfp4"):
             for k, n in SWEEP_KN:
                 print(json.dumps({"case": case, **_gemm(case, m, n, k, a.warmup, a.iters, g, dev, a.epi)}), flush=True)
+        return
+    elif a.case == "exchange_2gpu":
+        _exchange_2gpu(a.m, a.heads, a.k, a.warmup, a.iters, g, dev)
         return
     elif a.case == "qk_rope":
         # q and k views of a packed [S, 3, H, 128] QKV buffer, in place
