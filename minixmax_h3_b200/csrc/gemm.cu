@@ -135,7 +135,7 @@ struct GemmArgs {
 // epilogue reads its whole share into registers (192 per thread through
 // setmaxnreg) and releases it before computing, and five scale slots let
 // the writers run up to five slabs ahead of the MMAs.
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EM = EM_STORE>
 struct Cfg {
   static constexpr bool NVF4_PAIR = KIND == KIND_NVF4 && PAIR == 2;
   static constexpr int BN = (KIND == KIND_I8 || PAIR == 2) ? 256 : 192;  // MMA N
@@ -148,6 +148,7 @@ struct Cfg {
   static constexpr int SF_SLOTS = NVF4_PAIR ? 5 : 2;  // NVFP4 scale slots in TMEM, one K slab each
   static constexpr int SF_WPQ = NVF4_PAIR ? 1 : 2;    // NVFP4 scale writer warps per TMEM lane quadrant
   static constexpr int OUT_BUFS = 2;                   // epilogue staging buffers per warp (32x32 bf16 each)
+  static_assert(EM >= EM_STORE && EM <= EM_SEQ2HEAD, "epilogue mode");
   static constexpr int TMEM_COLS = 512;
   static constexpr int SF_STAGE_BYTES = KIND == KIND_NVF4 ? SFA_BYTES + SFB_BYTES : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE_BYTES;
@@ -187,9 +188,9 @@ static_assert(4 * REGS_CTL + 4 * REGS_SFW + 8 * REGS_EPI <= 16 * PAIR_LAUNCH_REG
 
 // TMEM column of NVFP4 scale slot `slot` (A scales at +4j, B scales at
 // +16+8j for K-step j).
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EM>
 H3B_DEV uint32_t sf_slot_col(int slot) {
-  return static_cast<uint32_t>(Cfg<KIND, PAIR>::SF_BASE + slot * SF_SLOT_COLS);
+  return static_cast<uint32_t>(Cfg<KIND, PAIR, EM>::SF_BASE + slot * SF_SLOT_COLS);
 }
 
 struct __align__(8) Barriers {
@@ -204,13 +205,15 @@ struct __align__(8) Barriers {
   int consumed;  // k-slabs whose full barrier the MMA thread has observed
 };
 
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EM = EM_STORE>
 constexpr size_t smem_bytes() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(Cfg<KIND, PAIR>::STAGES) * Cfg<KIND, PAIR>::STAGE_BYTES +
-         EPI_WARPS * Cfg<KIND, PAIR>::OUT_BUFS * OUT_STAGE_BYTES + sizeof(Barriers);
+  using C = Cfg<KIND, PAIR, EM>;
+  return 1024 /*alignment slack*/ + static_cast<size_t>(C::STAGES) * C::STAGE_BYTES +
+         EPI_WARPS * C::OUT_BUFS * OUT_STAGE_BYTES + sizeof(Barriers);
 }
 static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>() <= 227 * 1024 &&
-                  smem_bytes<KIND_I8, 1>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 2>() <= 227 * 1024,
+                  smem_bytes<KIND_I8, 1>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 2>() <= 227 * 1024 &&
+                  smem_bytes<KIND_NVF4, 2, EM_SEQ2HEAD>() <= 227 * 1024 && smem_bytes<KIND_I8, 2, EM_SEQ2HEAD>() <= 227 * 1024,
               "shared memory budget");
 
 // Lane 0 waits, the verdict is broadcast so the whole warp stays converged.
@@ -227,11 +230,11 @@ H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* a
 H3B_DEV uint32_t swz64(int r, int c) { return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
 template <int KIND, int PAIR, int EM>
-__global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
+__global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ PeerMaps peers,
                 const GemmArgs args) {
-  using C = Cfg<KIND, PAIR>;
+  using C = Cfg<KIND, PAIR, EM>;
   constexpr int BN = C::BN;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -429,7 +432,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
             }
           } else {
             // full[s] also means: this slab's scales are in TMEM slot it % SF_SLOTS
-            const uint32_t sf_col = tmem_base + sf_slot_col<KIND, PAIR>(slot);
+            const uint32_t sf_col = tmem_base + sf_slot_col<KIND, PAIR, EM>(slot);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               if constexpr (PAIR == 2)
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR>(it % C::SF_SLOTS);
+      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR, EM>(it % C::SF_SLOTS);
       tmem_st16(t, ra);
       tmem_st32(t + 16, rb);
       tc_wait_st();
@@ -570,7 +573,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR>(it & 1);
+      const uint32_t t = tmem_base + lane_off + sf_slot_col<KIND, PAIR, EM>(it & 1);
       tmem_st16(t, ra);
       tmem_st32(t + 16, rb);
       tc_wait_st();
@@ -837,7 +840,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR>::THREADS, 1)
 template <int KIND, int PAIR, int EM>
 int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_row_bytes, const GemmArgs& args,
                   cudaStream_t st, const PeerMaps* peer_maps) {
-  using C = Cfg<KIND, PAIR>;
+  using C = Cfg<KIND, PAIR, EM>;
   CUtensorMap ta, tb, ty;
   int rc = h3b::encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, a_row_bytes, args.m, a_row_bytes, 128, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B);
@@ -854,7 +857,7 @@ int launch_gemm_t(const void* a, const void* b, int64_t a_row_bytes, int64_t b_r
   } else {
     ty = ta;  // the int32 and scatter paths never use this map
   }
-  const size_t smem = smem_bytes<KIND, PAIR>();
+  const size_t smem = smem_bytes<KIND, PAIR, EM>();
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(gemm_kernel<KIND, PAIR, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
