@@ -51,6 +51,13 @@ def test_library_exports_every_symbol():
     ("h3b_gemm_i8_bf16", (16, 16, 16, 16, None, 16, 64, None, None, 0, None, None, 2, 4, 64, 128, None), 8),  # gate
     ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 256, None, None, 0, None, None, 0, 4, 256, 128, None), 1),
     ("h3b_quant_nvfp4", (16, 4, 48, 48, 16, 16, 16, 16, 1, None), 1),                       # k % 64
+    ("h3b_quant_nvfp4_gelu", (None, 4, 64, 64, 16, 16, 16, 16, 0, None), 8),                # null y
+    ("h3b_quant_nvfp4_gelu", (16, 4, 48, 48, 16, 16, 16, 16, 0, None), 1),                  # k % 64
+    ("h3b_quant_nvfp4_gelu", (16, 0, 64, 64, 16, 16, 16, 16, 0, None), 1),                  # needs a row
+    ("h3b_quant_nvfp4_gelu", (16, 4, 64, 64, 16, 16, 18, 16, 0, None), 2),                  # sf unaligned
+    ("h3b_gelu_amax_scan", (None, 4, 64, 64, 16, None), 8),                                  # null y
+    ("h3b_gelu_amax_scan", (16, 4, 60, 64, 16, None), 1),                                    # k % 8
+    ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 256, None, None, 0, None, None, 5, 4, 256, 256, None), 8),  # epi 5
     ("h3b_attention_fwd", (None,) * 6 + (1, 1, 1, 128, 128, 128, 128, 128, 128, 0.1, None), 8),
     ("h3b_attention_fwd", (16,) * 4 + (None, None, 1, 1, 1, 100, 128, 128, 128, 128, 128, 0.1, None), 2),
     ("h3b_rmsnorm_modulate", (16, 16, 4, 100, 100, 16, 16, 16, 0, None, 1e-6, None, None), 1),
@@ -78,6 +85,8 @@ def test_host_side_validation(name, args, code):
     ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 192, None, None, 0, None, None, 0, 0, 192, 256, None)),
     ("h3b_attention_fwd", (16,) * 4 + (None, None, 2, 0, 128, 128, 128, 128, 128, 128, 128, 0.1, None)),
     ("h3b_quant_i8_rows", (16, 0, 0, 64, 64, 16, 16, None)),
+    ("h3b_gelu_amax_scan", (16, 0, 64, 64, 16, None)),
+    ("h3b_gemm_nvfp4_bf16", (16,) * 6 + (None, 16, 256, None, None, 0, None, None, 4, 0, 256, 256, None)),  # posmax
 ])
 def test_empty_batch_is_a_no_op(name, args):
     """Zero rows: H3B_OK before any launch (the reference returns an empty
