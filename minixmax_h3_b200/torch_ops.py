@@ -9,6 +9,8 @@ kernel of the path:
     h3b::quant_i8_rows(x, convrot_group) -> (q int8 [m, k], scale fp32 [m])
     h3b::gemm_i8(q, xs, w, ws, bias, epilogue) -> y bf16 [m, n] ([m, n/2] SwiGLU)
     h3b::quant_nvfp4(x, hi_first) -> (codes u8 [m, k/2], blocked scales u8, gs fp32 [1])
+    h3b::gelu_amax_scan(y, ymax2) -> None  (updates ymax2[1]; see ops.gelu_amax_scan)
+    h3b::quant_nvfp4_gelu(y, ymax2, hi_first) -> (codes, blocked scales, gs) of bf16(gelu(y))
     h3b::gemm_nvfp4(a_codes, a_sf, a_gs, w_codes, w_sf, w_gs, bias, epilogue) -> y bf16
     h3b::attention(q, k, v, scale) -> o bf16 [S, H, 128]          (token-major)
     h3b::attention_bnsd(q, k, v, scale) -> o bf16 [1, H, S, 128]  (h3_attention_bnsd)
@@ -20,7 +22,8 @@ Each is registered for CUDA tensors only, so tensors on any other device raise
 (there is no CPU fallback).  Each forwards to the ``ops`` function of the same
 name, where a failing status code becomes a RuntimeError.  Each has a fake
 implementation giving the output shapes and dtypes without running anything.
-The operators write only fresh outputs (``mutates_args=()``), so the epilogue
+The operators write only fresh outputs (``mutates_args=()``; gelu_amax_scan
+declares the one fp32 pair it updates), so the epilogue
 that updates a residual in place (EPI_GATE_RES) is refused here; the modules
 use it through ``ops`` directly.  NVFP4 operands are in the tensor cores'
 nibble order (``ops.quant_nvfp4(hi_first=False)``, ``QuantLinear.prepare_cube``).
@@ -69,6 +72,16 @@ def _quant_nvfp4(x: torch.Tensor, hi_first: bool = False) -> tuple[torch.Tensor,
     return t.codes, t.sf, t.gs
 
 
+def _gelu_amax_scan(y: torch.Tensor, ymax2: torch.Tensor) -> None:
+    ops.gelu_amax_scan(y, ymax2)
+
+
+def _quant_nvfp4_gelu(y: torch.Tensor, ymax2: torch.Tensor,
+                      hi_first: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    t = ops.quant_nvfp4_gelu(y, ymax2, hi_first=hi_first)
+    return t.codes, t.sf, t.gs
+
+
 def _gemm_nvfp4(a_codes: torch.Tensor, a_sf: torch.Tensor, a_gs: torch.Tensor, w_codes: torch.Tensor,
                 w_sf: torch.Tensor, w_gs: torch.Tensor, bias: Optional[torch.Tensor] = None,
                 epilogue: int = 0) -> torch.Tensor:
@@ -107,6 +120,10 @@ quant_i8_rows = torch.library.custom_op("h3b::quant_i8_rows", mutates_args=(), d
 gemm_i8 = torch.library.custom_op("h3b::gemm_i8", mutates_args=(), device_types="cuda")(_gemm_i8)
 quant_nvfp4 = torch.library.custom_op("h3b::quant_nvfp4", mutates_args=(), device_types="cuda")(_quant_nvfp4)
 gemm_nvfp4 = torch.library.custom_op("h3b::gemm_nvfp4", mutates_args=(), device_types="cuda")(_gemm_nvfp4)
+gelu_amax_scan = torch.library.custom_op("h3b::gelu_amax_scan", mutates_args=("ymax2",),
+                                         device_types="cuda")(_gelu_amax_scan)
+quant_nvfp4_gelu = torch.library.custom_op("h3b::quant_nvfp4_gelu", mutates_args=(),
+                                           device_types="cuda")(_quant_nvfp4_gelu)
 attention = torch.library.custom_op("h3b::attention", mutates_args=(), device_types="cuda")(_attention)
 attention_bnsd = torch.library.custom_op("h3b::attention_bnsd", mutates_args=(),
                                          device_types="cuda")(_attention_bnsd)
@@ -133,6 +150,18 @@ def _(x, hi_first=False):
     sf_bytes = ops.sf_blocked_bytes(m, k) if m else 0
     return (x.new_empty((m, k // 2), dtype=torch.uint8), x.new_empty((sf_bytes,), dtype=torch.uint8),
             x.new_empty((1,), dtype=torch.float32))
+
+
+@gelu_amax_scan.register_fake
+def _(y, ymax2):
+    return None
+
+
+@quant_nvfp4_gelu.register_fake
+def _(y, ymax2, hi_first=False):
+    m, k = _rows_of(y), y.shape[-1]
+    return (y.new_empty((m, k // 2), dtype=torch.uint8), y.new_empty((ops.sf_blocked_bytes(m, k),), dtype=torch.uint8),
+            y.new_empty((1,), dtype=torch.float32))
 
 
 @gemm_nvfp4.register_fake

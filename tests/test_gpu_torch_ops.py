@@ -48,6 +48,17 @@ def test_nvfp4_operators(cuda):
     wq = ops.quant_nvfp4(w, hi_first=False)
     y = torch.ops.h3b.gemm_nvfp4(c, sf, gs, wq.codes, wq.sf, wq.gs, None, ops.EPI_STORE)
     assert torch.equal(y, ops.gemm_nvfp4(a, wq))
+    # the GELU MLP's fused activation + quantisation, against the ops calls
+    ymax2 = torch.zeros(2, dtype=torch.float32, device=cuda)
+    ymax2[0] = y.float().max().clamp(min=0.0)
+    torch.ops.h3b.gelu_amax_scan(y, ymax2)
+    cg, sfg, gsg = torch.ops.h3b.quant_nvfp4_gelu(y, ymax2, False)
+    ref2 = torch.zeros_like(ymax2)
+    ref2[0] = ymax2[0]
+    ops.gelu_amax_scan(y, ref2)
+    assert torch.equal(ymax2, ref2)
+    u = ops.quant_nvfp4_gelu(y, ref2)
+    assert torch.equal(cg, u.codes) and torch.equal(sfg, u.sf) and torch.equal(gsg, u.gs)
 
 
 def test_attention_and_norm_operators(cuda):

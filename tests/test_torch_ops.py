@@ -16,7 +16,7 @@ from minixmax_h3_b200 import torch_ops as T
 
 BF16, I8, U8, F32 = torch.bfloat16, torch.int8, torch.uint8, torch.float32
 OPS = ("quant_i8_rows", "gemm_i8", "quant_nvfp4", "gemm_nvfp4", "attention", "attention_bnsd",
-       "rmsnorm_modulate", "rmsnorm_modulate_quant_i8")
+       "rmsnorm_modulate", "rmsnorm_modulate_quant_i8", "gelu_amax_scan", "quant_nvfp4_gelu")
 
 
 def test_registered_and_refused_on_cpu():
