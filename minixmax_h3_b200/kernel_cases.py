@@ -5,6 +5,7 @@
     python -m minixmax_h3_b200.kernel_cases gemm_i8 --m 8192 --n 9216 --k 3072
     python -m minixmax_h3_b200.kernel_cases gemm_sweep --warmup 3 --iters 20   # cfg 2 + cfg 3 shapes, M 32768
     python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 3072
+    python -m minixmax_h3_b200.kernel_cases quant_nvfp4 --m 32768 --k 12288 --epi gelu   # GELU on load
     python -m minixmax_h3_b200.kernel_cases quant_i8 --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases quant_i8_convrot --m 32768 --k 3072
     python -m minixmax_h3_b200.kernel_cases qk_rope --seq 131072 --heads 24
@@ -124,7 +125,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=3072)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--iters", type=int, default=2)
-    ap.add_argument("--epi", choices=sorted(EPILOGUES), default="store", help="GEMM epilogue")
+    ap.add_argument("--epi", choices=sorted(EPILOGUES), default="store",
+                    help="GEMM epilogue; with quant_nvfp4, gelu quantises gelu(x) (the MLP fc2 input)")
     ap.add_argument("--layout", choices=["separate", "packed"], default="separate",
                     help="attention: separate [S, H, 128] tensors or views of a packed [S, 3, H, 128] QKV")
     a = ap.parse_args()
@@ -192,7 +194,14 @@ def main() -> None:
         rec.update(m=a.m, k=a.k, ms=ms, gbs=nbytes / ms / 1e6, bytes=nbytes)
     else:
         x = torch.randn(a.m, a.k, generator=g, device=dev).to(torch.bfloat16)
-        if a.case == "quant_nvfp4":
+        if a.case == "quant_nvfp4" and a.epi == "gelu":
+            # fc2's input quantiser with the MLP's GELU applied on load (x plays fc1's output y)
+            ymax2 = torch.zeros(2, dtype=torch.float32, device=dev)
+            ymax2[0] = x.float().max().clamp(min=0.0)
+            ops.gelu_amax_scan(x, ymax2)
+            ms = _time(lambda: ops.quant_nvfp4_gelu(x, ymax2), a.warmup, a.iters)
+            nbytes = 2 * a.m * a.k + a.m * a.k // 2 + a.m * a.k // 16
+        elif a.case == "quant_nvfp4":
             amax = ops.amax(x)
             ms = _time(lambda: ops.quant_nvfp4(x, amax_t=amax), a.warmup, a.iters)
             nbytes = 2 * a.m * a.k + a.m * a.k // 2 + a.m * a.k // 16
