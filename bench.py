@@ -354,6 +354,24 @@ def _phase_table(spans: list, steps: int) -> tuple[list[str], list[float]]:
     return names, [tot[n] / steps for n in names]
 
 
+def gemm_sweep_fracs(dev) -> dict:
+    """BASELINE cfg 2 / cfg 3: the INT8 and NVFP4 projection GEMMs at M = 32768
+    over the (K, N) of the four projections (kernel_cases gemm_sweep), each
+    timed by CUDA events over 10 launches after 3 warm-up ones, against the
+    B200 dense spec (this pool has no measured INT8 or FP4 peak).  Runs after
+    the timed steps, on one GPU."""
+    from minixmax_h3_b200.kernel_cases import SWEEP_KN, _gemm
+    g = torch.Generator(device=dev).manual_seed(0)
+    out: dict = {"m": 32768, "epilogue": "store", "int8": [], "nvfp4": []}
+    for case, key, peak, unit in (("gemm_i8", "int8", 4500.0, "TOP/s"), ("gemm_nvfp4", "nvfp4", 9000.0, "TFLOP/s")):
+        for k, n in SWEEP_KN:
+            r = _gemm(case, 32768, n, k, 3, 10, g, dev)
+            out[key].append({"n": n, "k": k, "ms": round(r["ms"], 4), "achieved": round(r["tflops"], 1),
+                             "unit": unit, "peak": peak, "frac": round(r["tflops"] / peak, 3)})
+    torch.cuda.synchronize()
+    return out
+
+
 def run_gpu(args) -> None:
     import torch.distributed as tdist
 
@@ -453,6 +471,7 @@ def run_gpu(args) -> None:
     clock = clocks.summary()
     # bit-exact sharded-vs-single-GPU and golden checks, on every rank
     parity = parity_check(ws, rank, dev)
+    sweep = gemm_sweep_fracs(dev) if ws == 1 else None
     torch.cuda.synchronize()
     status = list(_lib.device_status(clear=False))
     stat_t = torch.tensor(status, dtype=torch.int64, device=dev)
@@ -489,6 +508,7 @@ def run_gpu(args) -> None:
                               "frac": g_flops / (g_ms / g_count * 1e-3) / 1e12 / 9000.0,
                               "peak_kind": "B200 dense FP4 spec (no measured FP4 peak on this pool)",
                               "launch_ms": g_ms / g_count, "launches": g_count},
+            "gemm_sweep": sweep,
             "phases": {"names": names, "ms_per_step_by_rank": [[round(v, 2) for v in r] for r in by_rank]},
             "parity": parity,
             "device_status": statuses,
