@@ -372,6 +372,32 @@ def gemm_sweep_fracs(dev) -> dict:
     return out
 
 
+def attention_cfg4(dev, peak: float) -> dict:
+    """BASELINE cfg 4's attention on one GPU: 131072 tokens, 24 heads x 128,
+    non-causal, q/k/v as views of one packed [S, 3, H, 128] buffer (the QKV
+    projection's layout), 3 launches after 1 warm-up, CUDA events; against the
+    measured sustained bf16 peak.  Runs after the timed steps."""
+    from minixmax_h3_b200 import ops
+    s, h = 131072, 24
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(s, 3, h, 128, generator=g, device=dev).to(torch.bfloat16)
+    o = torch.empty(s, h, 128, dtype=torch.bfloat16, device=dev)
+    run = lambda: ops.attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], out=o)  # noqa: E731
+    run()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(3):
+        run()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 3
+    tflops = 4.0 * s * s * 128 * h / (ms * 1e-3) / 1e12
+    del qkv, o
+    return {"seq": s, "heads": h, "ms": round(ms, 3), "achieved": round(tflops, 1), "unit": "TFLOP/s",
+            "peak": peak, "frac": round(tflops / peak, 3)}
+
+
 def run_gpu(args) -> None:
     import torch.distributed as tdist
 
@@ -472,6 +498,7 @@ def run_gpu(args) -> None:
     # bit-exact sharded-vs-single-GPU and golden checks, on every rank
     parity = parity_check(ws, rank, dev)
     sweep = gemm_sweep_fracs(dev) if ws == 1 else None
+    attn4 = attention_cfg4(dev, peaks()["bf16"]) if ws == 1 else None
     torch.cuda.synchronize()
     status = list(_lib.device_status(clear=False))
     stat_t = torch.tensor(status, dtype=torch.int64, device=dev)
@@ -509,6 +536,7 @@ def run_gpu(args) -> None:
                               "peak_kind": "B200 dense FP4 spec (no measured FP4 peak on this pool)",
                               "launch_ms": g_ms / g_count, "launches": g_count},
             "gemm_sweep": sweep,
+            "attention_cfg4": attn4,
             "phases": {"names": names, "ms_per_step_by_rank": [[round(v, 2) for v in r] for r in by_rank]},
             "parity": parity,
             "device_status": statuses,
