@@ -230,6 +230,9 @@ def _config(ws: int) -> dict:
 # ----------------------------------------------------------------------------- GPU leg
 
 
+# every sequence-parallel scheme of block.Attention: p2p (the default, benched), nccl and
+# allgather bit-exact against one GPU, ring (fp32 chunk merge) within its test's bar
+SEQ_PARALLEL_SCHEMES = ("p2p", "nccl", "allgather", "ring")
 PARITY_CFG = {"hidden": 1024, "heads": 8, "ffn": 4096, "depth": 2, "text_dim": 1024, "n_text": 64,
               "grid": (4, 16, 63)}  # 64 text + 4032 video = 4096 tokens; 8 heads shard over up to 8 ranks
 
@@ -237,11 +240,15 @@ PARITY_CFG = {"hidden": 1024, "heads": 8, "ffn": 4096, "depth": 2, "text_dim": 1
 def parity_check(ws: int, rank: int, dev: torch.device) -> dict:
     """Runs on every rank, after the timed steps.
 
-    1. Sharded vs one GPU (N > 1): a small P2P-Ulysses step (PARITY_CFG, two
-       blocks, NVFP4 and INT8 linears) runs sharded over the N ranks; rank 0
-       gathers the outputs and compares them, bit for bit, with the same step
-       run on rank 0 alone.  The NVFP4 global scales are max-reduced across
-       ranks, so the sharded step quantises exactly as the single-GPU one.
+    1. Sharded vs one GPU (N > 1): a small Ulysses step (PARITY_CFG, two
+       blocks, NVFP4 and INT8 linears) runs sharded over the N ranks with each
+       sequence-parallel scheme (SEQ_PARALLEL_SCHEMES); rank 0 gathers the
+       outputs and compares them with the same step run on rank 0 alone: bit
+       for bit for p2p, nccl and allgather (the NVFP4 global scales are
+       max-reduced across ranks, so a sharded step quantises exactly as the
+       single-GPU one); for ring (chunk results merged in fp32) the two-GPU
+       test's bar, max relative error <= 0.1 and cosine >= 0.9999, is
+       reported.
     2. Golden (rank 0): a DiT block built from the weights of the committed
        golden fixture tests/golden/dit_block_nvfp4_gelu.pt, which the
        reference's own DiTBlock (model/dit.py:400-438) produced, must match the
@@ -270,35 +277,45 @@ def parity_check(ws: int, rank: int, dev: torch.device) -> dict:
     v0 = s0 + n_text_here - c["n_text"]
     video_local = video[v0:v0 + s_local - n_text_here]
     exact: dict = {}
-    for fmt in ("nvfp4", "int8_tensorwise"):
-        step = DiTStep(hidden=c["hidden"], heads=c["heads"], ffn=c["ffn"], depth=c["depth"], text_dim=c["text_dim"],
-                       fmt=fmt, mlp_act="gelu", device=dev, seq_parallel="p2p")
-        step.init_random(seed=5)  # identical weights on every rank
-        with torch.no_grad():
-            y_local = step(video_local.clone(), text, ts, rope)
-            if ws > 1:
+    ring: dict = {}
+    for fmt in ("nvfp4", "int8_tensorwise") if ws > 1 else ():
+        y_one = None
+        for scheme in SEQ_PARALLEL_SCHEMES:
+            step = DiTStep(hidden=c["hidden"], heads=c["heads"], ffn=c["ffn"], depth=c["depth"],
+                           text_dim=c["text_dim"], fmt=fmt, mlp_act="gelu", device=dev, seq_parallel=scheme)
+            step.init_random(seed=5)  # identical weights on every rank and for every scheme
+            with torch.no_grad():
+                y_local = step(video_local.clone(), text, ts, rope)
                 parts = [torch.empty_like(y_local) for _ in range(ws)]
                 tdist.all_gather(parts, y_local)
                 if rank == 0:
-                    st = hdist.state()
-                    hdist.set_state(0, 1)  # the same step on this GPU alone
-                    try:
-                        y_one = step(video.clone(), text, ts, rope)
-                    finally:
-                        hdist.set_state(st.rank, st.world_size, local_rank=st.local_rank, group=st.group,
-                                        backend=st.backend)
+                    if y_one is None:
+                        st = hdist.state()
+                        hdist.set_state(0, 1)  # the same step on this GPU alone
+                        try:
+                            y_one = step(video.clone(), text, ts, rope)
+                        finally:
+                            hdist.set_state(st.rank, st.world_size, local_rank=st.local_rank, group=st.group,
+                                            backend=st.backend)
                     y_sp = torch.cat(parts)
-                    exact[fmt] = bool(torch.equal(y_sp, y_one))
-                    if not exact[fmt]:
-                        d = (y_sp.float() - y_one.float()).abs()
-                        exact[f"{fmt}_max_abs"] = d.max().item()
+                    if scheme == "ring":  # chunk results merged in fp32, then re-quantised: the test bar
+                        g_, w_ = y_sp.float().reshape(-1), y_one.float().reshape(-1)
+                        err = ((g_ - w_).abs() / w_.abs().clamp(min=1.0)).max().item()
+                        cos = torch.nn.functional.cosine_similarity(g_.double(), w_.double(), dim=0).item()
+                        ring[fmt] = {"max_rel_err": err, "cosine": cos, "ok": err <= 0.1 and cos >= 0.9999}
+                    else:
+                        key = fmt if scheme == "p2p" else f"{fmt}/{scheme}"
+                        exact[key] = bool(torch.equal(y_sp, y_one))
+                        if not exact[key]:
+                            exact[f"{key}_max_abs"] = (y_sp.float() - y_one.float()).abs().max().item()
                 tdist.barrier(device_ids=[dev.index])
-        del step
+            del step
     if ws > 1:
         out["sharded_vs_one_gpu"] = {"exact": all(v for k, v in exact.items() if not k.endswith("_max_abs"))
-                                     if rank == 0 else None, "formats": exact, "tokens": s_total,
-                                     "hidden": c["hidden"], "heads": c["heads"], "blocks": c["depth"],
-                                     "scheme": "p2p"}
+                                     if rank == 0 else None, "formats": exact,
+                                     "ring_within_bar": all(r["ok"] for r in ring.values()) if rank == 0 else None,
+                                     "ring": ring, "tokens": s_total, "hidden": c["hidden"], "heads": c["heads"],
+                                     "blocks": c["depth"], "schemes": list(SEQ_PARALLEL_SCHEMES)}
     else:
         out["sharded_vs_one_gpu"] = None  # one GPU: nothing is sharded
     if rank == 0:
@@ -550,8 +567,10 @@ def run_gpu(args) -> None:
         barrier()
     hdist.destroy()
     bad = [s for s in statuses if s[0] != 0]
-    failed = rank == 0 and (bad or (parity.get("sharded_vs_one_gpu") or {}).get("exact") is False
-                            or not parity["golden"]["ok"])
+    # p2p / nccl / allgather must be bit-exact; the ring's float bar is reported, not enforced here (its
+    # NVFP4 re-quantisation of the fp32-merged rows sits near it; tests/test_gpu_ulysses.py enforces it)
+    sharded = parity.get("sharded_vs_one_gpu") or {}
+    failed = rank == 0 and (bad or sharded.get("exact") is False or not parity["golden"]["ok"])
     if failed:
         raise SystemExit(f"bench: device status {statuses} / parity {parity}")
 
