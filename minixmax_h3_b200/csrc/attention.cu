@@ -112,9 +112,10 @@ struct AttnArgs {
   float scale_log2;
 };
 
+template <bool SPIN = false>
 H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
   int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait<SPIN>(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -313,84 +314,95 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // (its waits poll without a suspend hint: it is the latency-critical
-    // hand-off from the softmax back to the tensor pipe)
-    if (lane == 0) {
-      bool ok = mbar_wait<true>(&bars->q_full, 0, &g_status, 3, abort_flag);
+    // The whole warp runs the schedule converged: lane 0 waits (polling
+    // without a suspend hint: this is the latency-critical hand-off from the
+    // softmax back to the tensor pipe) and broadcasts the verdict, every lane
+    // computes the descriptors, and one elected lane issues each batch of
+    // tcgen05.mma and its commit.
+    bool ok = warp_wait<true>(&bars->q_full, 0, 3, abort_flag);
+    tc_fence_after();
+    // k_full[j % 2] completes once per use of the slot; its next phase is
+    // K_{j+2}, loaded only after kv_free(j), which this warp commits later
+    // (behind S_0(j+1)): one phase behind.  Likewise v_full[j % 3] (next:
+    // V_{j+3}, after kv_free(j+1)).  K_{j+1} is waited for in iteration j,
+    // after kv_free(j-1) released the slot it is loaded into.
+    auto wait_k = [&](int j) -> bool {
+      if (!warp_wait<true>(&bars->k_full[j % KST], (j / KST) & 1, 4, abort_flag)) return false;
       tc_fence_after();
-      // k_full[j % 2] completes once per use of the slot; its next phase is
-      // K_{j+2}, loaded only after kv_free(j), which this thread commits
-      // later (behind S_0(j+1)): one phase behind.  Likewise v_full[j % 3]
-      // (next: V_{j+3}, after kv_free(j+1)).  K_{j+1} is waited for in
-      // iteration j, after kv_free(j-1) released the slot it is loaded into.
-      auto wait_k = [&](int j) -> bool {
-        if (!mbar_wait<true>(&bars->k_full[j % KST], (j / KST) & 1, &g_status, 4, abort_flag)) return false;
-        tc_fence_after();
-        return true;
-      };
-      auto wait_v = [&](int j) -> bool {
-        if (!mbar_wait<true>(&bars->v_full[j % VST], (j / VST) & 1, &g_status, 6, abort_flag)) return false;
-        tc_fence_after();
-        return true;
-      };
-      // S_i = Q_i K_j^T (fresh accumulator), then publish it.  K-major Q/K
-      // tiles advance 32 bytes (encoded 2) per 16-wide K step inside a
-      // 64-column half and a half tile (16 KB) every 4 steps: a descriptor
-      // step moves only the start-address field (desc_add_lo).
-      auto issue_s = [&](int i, int j) {
-        const uint32_t d = tmem + s_col(i);
-        const uint64_t qd = sdesc_kmajor_sw128(smem_u32(sQ + i * Q_TILE_BYTES));
-        const uint64_t kd = sdesc_kmajor_sw128(smem_u32(sK + (j % KST) * KV_TILE_BYTES));
+      return true;
+    };
+    auto wait_v = [&](int j) -> bool {
+      if (!warp_wait<true>(&bars->v_full[j % VST], (j / VST) & 1, 6, abort_flag)) return false;
+      tc_fence_after();
+      return true;
+    };
+    auto commit = [&](uint64_t* bar) {
+      if (elect_one()) tc_commit(bar);
+      __syncwarp();
+    };
+    // S_i = Q_i K_j^T (fresh accumulator), then publish it.  K-major Q/K
+    // tiles advance 32 bytes (encoded 2) per 16-wide K step inside a
+    // 64-column half and a half tile (16 KB) every 4 steps: a descriptor
+    // step moves only the start-address field (desc_add_lo).
+    auto issue_s = [&](int i, int j) {
+      const uint32_t d = tmem + s_col(i);
+      const uint64_t qd = sdesc_kmajor_sw128(smem_u32(sQ + i * Q_TILE_BYTES));
+      const uint64_t kd = sdesc_kmajor_sw128(smem_u32(sK + (j % KST) * KV_TILE_BYTES));
+      if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t step = static_cast<uint32_t>((kk >> 2) * (Q_HALF_BYTES >> 4) + (kk & 3) * 2);
           mma_f16_ss(d, desc_add_lo(qd, step), desc_add_lo(kd, step), IDESC_S, kk > 0);
         }
         tc_commit(&bars->s_full[i]);
-      };
-      // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  Each
-      // p_half[i][h] completes once per tile; the softmax cannot arrive for
-      // j+1 before S_i(j+1), which is issued after these waits, so each wait
-      // is one phase behind.  P is published in two halves (K/V rows 0-63,
-      // 64-127) so the first half of P.V runs while the softmax computes the
-      // second.  The MN-major V tile advances 2048 bytes per 16 keys.
-      auto issue_pv = [&](int i, int j) -> bool {
-        const uint32_t p_tmem = tmem + s_col(i);
-        const uint32_t o_tmem = tmem + o_col(i);
-        const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(sV + (j % VST) * KV_TILE_BYTES), KV_HALF_BYTES, 1024);
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait<true>(&bars->p_half[i][h], j & 1, &g_status, 7, abort_flag)) return false;
-          tc_fence_after();
+      }
+      __syncwarp();
+    };
+    // O_i (+)= P_i(j) V_j once the softmax has written P_i(j).  Each
+    // p_half[i][h] completes once per tile; the softmax cannot arrive for
+    // j+1 before S_i(j+1), which is issued after these waits, so each wait
+    // is one phase behind.  P is published in two halves (K/V rows 0-63,
+    // 64-127) so the first half of P.V runs while the softmax computes the
+    // second.  The MN-major V tile advances 2048 bytes per 16 keys.
+    auto issue_pv = [&](int i, int j) -> bool {
+      const uint32_t p_tmem = tmem + s_col(i);
+      const uint32_t o_tmem = tmem + o_col(i);
+      const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(sV + (j % VST) * KV_TILE_BYTES), KV_HALF_BYTES, 1024);
+      for (int h = 0; h < 2; ++h) {
+        if (!warp_wait<true>(&bars->p_half[i][h], j & 1, 7, abort_flag)) return false;
+        tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 4 * h; kk < 4 * h + 4; ++kk)
             mma_f16_ts(o_tmem, p_tmem + kk * 8, desc_add_lo(vd, static_cast<uint32_t>(kk * (2048 >> 4))),
                        IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        return true;
-      };
-      ok = ok && wait_k(0);
-      if (ok) {
-        issue_s(0, 0);
-        issue_s(1, 0);
+        __syncwarp();
       }
-      ok = ok && wait_v(0) && (n_kv == 1 || wait_k(1)) && issue_pv(0, 0);
-      for (int j = 1; j < n_kv && ok; ++j) {
-        issue_s(0, j);                          // behind PV0(j-1) in the pipe
-        tc_commit(&bars->kv_free[(j - 1) & 1]);  // K_{j-1} and V_{j-2} no longer read
-        if (!issue_pv(1, j - 1)) {              // PV1(j-1)
-          ok = false;
-          break;
-        }
-        issue_s(1, j);                          // behind PV1(j-1)
-        if (!wait_v(j) || (j + 1 < n_kv && !wait_k(j + 1)) || !issue_pv(0, j)) {
-          ok = false;
-          break;
-        }
-      }
-      if (ok && issue_pv(1, n_kv - 1)) tc_commit(&bars->o_done);
-      tc_commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
+      return true;
+    };
+    ok = ok && wait_k(0);
+    if (ok) {
+      issue_s(0, 0);
+      issue_s(1, 0);
     }
+    ok = ok && wait_v(0) && (n_kv == 1 || wait_k(1)) && issue_pv(0, 0);
+    for (int j = 1; j < n_kv && ok; ++j) {
+      issue_s(0, j);                    // behind PV0(j-1) in the pipe
+      commit(&bars->kv_free[(j - 1) & 1]);  // K_{j-1} and V_{j-2} no longer read
+      if (!issue_pv(1, j - 1)) {        // PV1(j-1)
+        ok = false;
+        break;
+      }
+      issue_s(1, j);                    // behind PV1(j-1)
+      if (!wait_v(j) || (j + 1 < n_kv && !wait_k(j + 1)) || !issue_pv(0, j)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && issue_pv(1, n_kv - 1)) commit(&bars->o_done);
+    commit(&bars->drain);
+    warp_wait(&bars->drain, 0, 8, nullptr);
   }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
