@@ -109,18 +109,28 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 8 : 1) rmsnorm_modul
     const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ shift,
     const __nv_bfloat16* __restrict__ scale, int64_t tab_ld, const int32_t* __restrict__ row_sel, float eps,
     float* __restrict__ amax_out) {
+  __shared__ h3b::RowSlots slots;
   __shared__ float red[33];
   const int nvec = static_cast<int>(hidden >> 3);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float amax = 0.0f;
-  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+  int64_t row = blockIdx.x;
+  uint4 nxt[MAXV] = {};
+  if (row < m) h3b::load_row<THREADS, MAXV>(x + row * ld, nvec, nxt);
+  for (int par = 0; row < m; row += gridDim.x, par ^= 1) {
+    uint4 v[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) v[i] = nxt[i];
+    // the next row's loads stay in flight while this one is worked on
+    if (row + gridDim.x < m) h3b::load_row<THREADS, MAXV>(x + (row + gridDim.x) * ld, nvec, nxt);
     const int sel = row_sel != nullptr ? row_sel[row] : 0;
     const bool modulate = sel >= 0;
     const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
-    uint4 v[MAXV];
-    amax = fmaxf(amax, h3b::rmsnorm_modulate_row<THREADS, MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r,
-                                                       modulate, red, v));
+    float a = h3b::rmsnorm_modulate_regs<THREADS, MAXV>(v, nvec, hidden, eps, w, shift_r, scale_r, modulate,
+                                                        slots.v[par]);
+    if (a != a) a = h3b::regs_amax<THREADS, MAXV>(v, nvec);  // NaNs are skipped in the reported max
+    amax = fmaxf(amax, a);
     __nv_bfloat16* hr = h + row * ld;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
@@ -265,9 +275,10 @@ extern "C" int h3b_rmsnorm_modulate(const void* x, void* h, int64_t m, int64_t h
   const auto* sh = static_cast<const __nv_bfloat16*>(shift);
   const auto* sc = static_cast<const __nv_bfloat16*>(scale);
   const int64_t nvec = hidden / 8;
-  // rows up to 3072 wide: 128-thread CTAs (8 per SM, one row each in flight)
+  // rows up to 3072 wide: 128-thread CTAs, 8 resident per SM, each with one
+  // row in work and the next one loading; the grid is one resident wave
   const bool narrow = nvec <= 128 * 3;
-  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * (narrow ? 16 : 8);
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * 8;
   if (blocks > m) blocks = m;
   const unsigned g = static_cast<unsigned>(blocks);
   if (narrow)

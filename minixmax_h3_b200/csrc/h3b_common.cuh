@@ -526,6 +526,15 @@ H3B_DEV float2 add2(float2 a, float2 b) {
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return d;
 }
+// Two round-to-nearest sums, bit-identical to two __fadd_rn (never fused
+// with a neighbouring product).
+H3B_DEV float2 add2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
 // Two round-to-nearest products, bit-identical to two __fmul_rn.
 H3B_DEV float2 mul2(float2 a, float2 b) {
   float2 d;

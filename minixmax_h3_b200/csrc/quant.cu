@@ -456,23 +456,33 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? (ROT ? 6 : 8) : 1) r
     const __nv_bfloat16* __restrict__ x, int64_t m, int64_t hidden, int64_t ld, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale, int64_t tab_ld,
     const int32_t* __restrict__ row_sel, float eps, int8_t* __restrict__ q, float* __restrict__ q_scale) {
+  __shared__ h3b::RowSlots sum_slots, max_slots;
   __shared__ float red[33];
   const int nvec = static_cast<int>(hidden >> 3);
-  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+  int64_t row = blockIdx.x;
+  uint4 nxt[MAXV] = {};
+  if (row < m) h3b::load_row<THREADS, MAXV>(x + row * ld, nvec, nxt);
+  for (int par = 0; row < m; row += gridDim.x, par ^= 1) {
+    uint4 v[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) v[i] = nxt[i];
+    // the next row's loads stay in flight while this one is worked on
+    if (row + gridDim.x < m) h3b::load_row<THREADS, MAXV>(x + (row + gridDim.x) * ld, nvec, nxt);
     const int sel = row_sel != nullptr ? row_sel[row] : 0;
     const bool modulate = sel >= 0;
     const __nv_bfloat16* shift_r = shift + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
     const __nv_bfloat16* scale_r = scale + static_cast<int64_t>(modulate ? sel : 0) * tab_ld;
-    uint4 v[MAXV];
-    float amax = h3b::rmsnorm_modulate_row<THREADS, MAXV>(x + row * ld, nvec, hidden, eps, w, shift_r, scale_r, modulate,
-                                                 red, v);
-    float f[MAXV][8];
+    // amax: NaN if any element of this thread's share is NaN
+    float amax = h3b::rmsnorm_modulate_regs<THREADS, MAXV>(v, nvec, hidden, eps, w, shift_r, scale_r, modulate,
+                                                           sum_slots.v[par]);
+    // ROT: the rotated row as floats; otherwise h is read from v directly
+    float f[ROT ? MAXV : 1][8];
+    if constexpr (ROT) {
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * THREADS;
-      if (vi < nvec) {  // warp-uniform when ROT (hidden % 256 == 0)
-        unpack8<__nv_bfloat16>(v[i], f[i]);
-        if constexpr (ROT) {
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = threadIdx.x + i * THREADS;
+        if (vi < nvec) {  // warp-uniform (hidden % 256 == 0)
+          unpack8<__nv_bfloat16>(v[i], f[i]);
           double d[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) d[e] = static_cast<double>(f[i][e]);
@@ -481,38 +491,86 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? (ROT ? 6 : 8) : 1) r
           for (int e = 0; e < 8; ++e) f[i][e] = __bfloat162float(f64_round<__nv_bfloat16>(d[e] * 0.0625));
         }
       }
-    }
-    if constexpr (ROT) {
       amax = 0.0f;
 #pragma unroll
       for (int i = 0; i < MAXV; ++i) {
         if (threadIdx.x + i * THREADS < nvec) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[i][e]));
+          for (int e = 0; e < 8; ++e) amax = h3b::fmax_nan(amax, fabsf(f[i][e]));
         }
       }
     }
-    amax = block_max<THREADS>(amax, red);
-    amax = fmaxf(amax, 1e-12f);
-    const float s = __fdiv_rn(amax, 127.0f);
-    const bool fast = rcp_div_ok_all(s);  // s >= 1e-12 / 127 > 2^-47
-    const float y = __frcp_rn(s);
-    int8_t* qr = q + row * hidden;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * THREADS;
-      if (vi < nvec) {
-        uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float fj = f[i][j];
-          float r = rintf(fast ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
-          r = fminf(fmaxf(r, -128.0f), 127.0f);
-          const uint32_t b = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
-          packed[j >> 2] |= b << ((j & 3) * 8);
-        }
-        *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * 8) = make_uint2(packed[0], packed[1]);
+    // The row max, NaN if the row holds a NaN (one barrier).  A finite row
+    // whose scale admits the reciprocal quotient everywhere takes the packed
+    // path; any other row the per-element path with NaNs skipped in the max.
+    auto elem = [&](int i, int j) -> float {
+      if constexpr (ROT) {
+        return f[i][j];
+      } else {
+        const uint32_t u = j < 2 ? v[i].x : j < 4 ? v[i].y : j < 6 ? v[i].z : v[i].w;
+        return (j & 1) ? bf16hi_to_f32(u) : bf16lo_to_f32(u);
       }
+    };
+    const float row_max = h3b::block_max_nan_1bar<THREADS>(amax, max_slots.v[par]);
+    float s = __fdiv_rn(fmaxf(row_max, 1e-12f), 127.0f);
+    int8_t* qr = q + row * hidden;
+    if (row_max <= 3.4028234663852886e38f && rcp_div_ok_all(s)) {
+      // q = rint(x / s) by Markstein's quotient (packed fp32x2, the same
+      // bits as div_rn_by_rcp) and the 1.5 * 2^23 rounding add, which
+      // leaves rint(q) in the low byte.  |x / s| <= 127 (1 + 2^-23) here,
+      // so the clamp to [-128, 127] never binds.
+      const float y = __frcp_rn(s);
+      const float2 y2 = make_float2(y, y), ns2 = make_float2(-s, -s);
+      const float2 magic2 = make_float2(0x1.8p23f, 0x1.8p23f);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = threadIdx.x + i * THREADS;
+        if (vi < nvec) {
+          uint32_t b[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f2 = make_float2(elem(i, 2 * e), elem(i, 2 * e + 1));
+            const float2 q0 = mul2(f2, y2);
+            const float2 qq = fma2(fma2(q0, ns2, f2), y2, q0);
+            const float2 t = add2_rn(qq, magic2);
+            b[2 * e] = __float_as_uint(t.x);
+            b[2 * e + 1] = __float_as_uint(t.y);
+          }
+          const uint32_t w0 = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+          const uint32_t w1 = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+          *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * 8) = make_uint2(w0, w1);
+        }
+      }
+    } else {
+      float a = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        if (threadIdx.x + i * THREADS < nvec) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(elem(i, e)));
+        }
+      }
+      a = block_max<THREADS>(a, red);
+      s = __fdiv_rn(fmaxf(a, 1e-12f), 127.0f);
+      const bool fast = rcp_div_ok_all(s);
+      const float y = __frcp_rn(s);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = threadIdx.x + i * THREADS;
+        if (vi < nvec) {
+          uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float fj = elem(i, j);
+            float r = rintf(fast ? div_rn_by_rcp(fj, s, y) : __fdiv_rn(fj, s));
+            r = fminf(fmaxf(r, -128.0f), 127.0f);
+            const uint32_t bj = static_cast<uint32_t>(static_cast<int32_t>(r)) & 0xFFu;
+            packed[j >> 2] |= bj << ((j & 3) * 8);
+          }
+          *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * 8) = make_uint2(packed[0], packed[1]);
+        }
+      }
+      __syncthreads();  // red[] is read by every thread above before the next row writes it
     }
     if (threadIdx.x == 0) q_scale[row] = s;
   }
@@ -667,9 +725,11 @@ extern "C" int h3b_rmsnorm_modulate_quant_i8(const void* x, int64_t m, int64_t h
   const auto* sh = static_cast<const __nv_bfloat16*>(shift);
   const auto* sc = static_cast<const __nv_bfloat16*>(scale);
   const int64_t nvec = hidden / 8;
-  // rows up to 3072 wide: 128-thread CTAs (8 per SM, one row each in flight)
+  // rows up to 3072 wide: 128-thread CTAs, 8 resident per SM (6 with
+  // ConvRot), each with one row in work and the next one loading; the grid
+  // is one resident wave
   const bool narrow = nvec <= 128 * 3;
-  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * (narrow ? 16 : 8);
+  int64_t blocks = static_cast<int64_t>(h3b::num_sms()) * (narrow ? (convrot_group == 256 ? 6 : 8) : 8);
   if (blocks > m) blocks = m;
   const unsigned g = static_cast<unsigned>(blocks);
   const bool rot = convrot_group == 256;
