@@ -18,43 +18,63 @@ namespace {
 
 // One warp per token; lane l owns d = 4l..4l+3 of every 128-element head
 // row.  The token's rotation (bf16 cos/sin of its 64 angles) is computed once
-// and applied to all heads of q and k, ROWS head rows in flight at a time.
-template <int ROWS>
+// and applied to all heads of q and k, four head rows in flight at a time.
+// The four rows' sums of squares are reduced together (a reduce-scatter over
+// lane bits 4 and 3, then a butterfly over bits 2-0: ten shuffles instead of
+// twenty), lanes 8u..8u+7 compute row u's rstd and pass it on, and the bf16
+// steps of the rotation run two elements per packed bf16x2 instruction: the
+// product of two bf16 values and the sum of two are exact in fp32, so each
+// packed result equals the reference's fp32 operation rounded to bf16.
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t s_len, int heads, int64_t seq_stride,
     int64_t head_stride, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
     const float* __restrict__ pos, int64_t pos_offset, const float* __restrict__ inv_freq, int n_t, int n_h) {
+  constexpr int ROWS = 4;
   const int lane = threadIdx.x & 31;
   const int64_t s = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (s >= s_len) return;  // warp-uniform
   // element j (lane < 16: j = 4*lane.. in the first half; lane >= 16: second half)
   const float* ps = pos + (pos_offset + s) * 3;
   const bool first = lane < 16;
-  float c[4], sn[4];
+  // bf16x2 cos and sin of the lane's four angles; the first half rotates by
+  // c*x[j] + (-s)*x[j+64], the second by s*x[j] + c*x[j+64], so the first
+  // half's sin is negated (bf16 rounding is symmetric).
+  uint32_t cw[2], sw[2];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int jj = (lane & 15) * 4 + e;  // frequency index 0..63
-    const int axis = jj < n_t ? 0 : (jj < n_t + n_h ? 1 : 2);
-    const float ang = __fmul_rn(ps[axis], inv_freq[jj]);
-    c[e] = bf16r(cosf(ang));
-    sn[e] = bf16r(sinf(ang));
+  for (int e = 0; e < 4; e += 2) {
+    float cc[2], ss[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int jj = (lane & 15) * 4 + e + t;  // frequency index 0..63
+      const int axis = jj < n_t ? 0 : (jj < n_t + n_h ? 1 : 2);
+      const float ang = __fmul_rn(ps[axis], inv_freq[jj]);
+      cc[t] = cosf(ang);
+      ss[t] = first ? -sinf(ang) : sinf(ang);
+    }
+    cw[e >> 1] = pack_bf16x2(cc[0], cc[1]);
+    sw[e >> 1] = pack_bf16x2(ss[0], ss[1]);
   }
-  float wq[4], wk[4];
+  float2 wq[2], wk[2];
   {
     const uint2 a = *reinterpret_cast<const uint2*>(qw + lane * 4);
-    wq[0] = bf16lo_to_f32(a.x), wq[1] = bf16hi_to_f32(a.x), wq[2] = bf16lo_to_f32(a.y), wq[3] = bf16hi_to_f32(a.y);
+    wq[0] = make_float2(bf16lo_to_f32(a.x), bf16hi_to_f32(a.x));
+    wq[1] = make_float2(bf16lo_to_f32(a.y), bf16hi_to_f32(a.y));
     if (k != nullptr) {
       const uint2 b = *reinterpret_cast<const uint2*>(kw + lane * 4);
-      wk[0] = bf16lo_to_f32(b.x), wk[1] = bf16hi_to_f32(b.x), wk[2] = bf16lo_to_f32(b.y), wk[3] = bf16hi_to_f32(b.y);
+      wk[0] = make_float2(bf16lo_to_f32(b.x), bf16hi_to_f32(b.x));
+      wk[1] = make_float2(bf16lo_to_f32(b.y), bf16hi_to_f32(b.y));
     }
   }
+  const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0;
   const int rows = heads * (k != nullptr ? 2 : 1);  // q heads, then k heads
   for (int r0 = 0; r0 < rows; r0 += ROWS) {
     uint2 raw[ROWS];
     __nv_bfloat16* base[ROWS];
+    float ssq[ROWS];
 #pragma unroll
     for (int u = 0; u < ROWS; ++u) {
       const int r = r0 + u;
+      raw[u] = make_uint2(0u, 0u);
       if (r < rows) {
         const bool is_k = r >= heads;
         const int h = is_k ? r - heads : r;
@@ -64,38 +84,43 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     }
 #pragma unroll
     for (int u = 0; u < ROWS; ++u) {
+      const float2 x01 = make_float2(bf16lo_to_f32(raw[u].x), bf16hi_to_f32(raw[u].x));
+      const float2 x23 = make_float2(bf16lo_to_f32(raw[u].y), bf16hi_to_f32(raw[u].y));
+      const float2 t = fma2(x23, x23, mul2(x01, x01));
+      ssq[u] = t.x + t.y;
+    }
+    // reduce-scatter: after xor 16 a lane holds rows 2*b4, 2*b4+1; after
+    // xor 8 row 2*b4+b3; xor 4, 2, 1 complete its sum in lanes 8u..8u+7
+    const float s0 = __shfl_xor_sync(0xffffffffu, b4 ? ssq[0] : ssq[2], 16);
+    const float s1 = __shfl_xor_sync(0xffffffffu, b4 ? ssq[1] : ssq[3], 16);
+    const float k0 = (b4 ? ssq[2] : ssq[0]) + s0;
+    const float k1 = (b4 ? ssq[3] : ssq[1]) + s1;
+    float tot = (b3 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 4);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+    // mean = tot / 128 (exact scaling), rstd = RN(1 / RN(sqrt(mean + eps)))
+    const float my_rstd = __frcp_rn(__fsqrt_rn(__fmul_rn(tot, 0.0078125f) + eps));
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
       const int r = r0 + u;
+      const float rstd = __shfl_sync(0xffffffffu, my_rstd, 8 * u);
       if (r >= rows) break;  // warp-uniform
-      const float* w = r >= heads ? wk : wq;
-      float x[4] = {bf16lo_to_f32(raw[u].x), bf16hi_to_f32(raw[u].x), bf16lo_to_f32(raw[u].y),
-                    bf16hi_to_f32(raw[u].y)};
-      float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-      ss = warp_sum(ss);
-      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, 128.0f) + eps));
-      float n[4];
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const float2 t = bf16r2(__fmul_rn(__fmul_rn(x[e], rstd), w[e]), __fmul_rn(__fmul_rn(x[e + 1], rstd), w[e + 1]));
-        n[e] = t.x;
-        n[e + 1] = t.y;
-      }
-      // partner element j +- 64 lives in lane +- 16, same slot
-      float p[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) p[e] = __shfl_xor_sync(0xffffffffu, n[e], 16);
-      // first half:  c*x[j] + (-s)*x[j+64];  second half: s*x[j] + c*x[j+64]
-      // (each product and the sum rounded to bf16; two elements per conversion)
+      const float2* w = r >= heads ? wk : wq;
+      const float2 r2 = make_float2(rstd, rstd);
+      const float2 x01 = make_float2(bf16lo_to_f32(raw[u].x), bf16hi_to_f32(raw[u].x));
+      const float2 x23 = make_float2(bf16lo_to_f32(raw[u].y), bf16hi_to_f32(raw[u].y));
+      const float2 n01 = mul2(mul2(x01, r2), w[0]);  // (x * rstd) * w, each product rounded
+      const float2 n23 = mul2(mul2(x23, r2), w[1]);
+      const uint32_t nb[2] = {pack_bf16x2(n01.x, n01.y), pack_bf16x2(n23.x, n23.y)};
+      // partner elements j +- 64 live in lane +- 16, same slots
       uint32_t ow[2];
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const float2 a = first ? bf16r2(c[e] * n[e], c[e + 1] * n[e + 1]) : bf16r2(sn[e] * p[e], sn[e + 1] * p[e + 1]);
-        const float2 b = first ? bf16r2(-sn[e] * p[e], -sn[e + 1] * p[e + 1]) : bf16r2(c[e] * n[e], c[e + 1] * n[e + 1]);
-        ow[e >> 1] = pack_bf16x2(a.x + b.x, a.y + b.y);
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t pb = __shfl_xor_sync(0xffffffffu, nb[e], 16);
+        ow[e] = h3b::bf16x2_add(h3b::bf16x2_mul(cw[e], nb[e]), h3b::bf16x2_mul(sw[e], pb));
       }
-      uint2 o;
-      o.x = ow[0];
-      o.y = ow[1];
-      *reinterpret_cast<uint2*>(base[u] + lane * 4) = o;
+      *reinterpret_cast<uint2*>(base[u] + lane * 4) = make_uint2(ow[0], ow[1]);
     }
   }
 }
@@ -251,7 +276,7 @@ extern "C" int h3b_qk_rmsnorm_rope(void* q, void* k, int64_t s, int64_t heads, i
   if (heads > 65535) return H3B_ERR_SHAPE;
   const int64_t blocks = (s + 7) / 8;  // one warp per token
   if (blocks > 0x7fffffff) return H3B_ERR_SHAPE;
-  qk_rmsnorm_rope_kernel<4><<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), s, static_cast<int>(heads), seq_stride,
       head_stride, static_cast<const __nv_bfloat16*>(q_weight), static_cast<const __nv_bfloat16*>(k_weight), eps,
       pos, pos_offset, inv_freq, n_t, n_h);

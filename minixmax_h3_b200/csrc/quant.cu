@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
     }
     float amax_b = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) amax_b = fmaxf(amax_b, fabsf(f[j]));
+    for (int j = 0; j < 16; j += 2) amax_b = fmax3(amax_b, fabsf(f[j]), fabsf(f[j + 1]));
     const float ratio = (six_ok && amax_b >= 0x1p-90f) ? div_rn_by_rcp(amax_b, six_gs, y6) : __fdiv_rn(amax_b, six_gs);
     const __nv_fp8_storage_t sb = __nv_cvt_float_to_fp8(ratio, __NV_SATFINITE, __NV_E4M3);
     const uint32_t sbits = static_cast<uint32_t>(sb) & 0xFFu;
@@ -395,8 +395,16 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* _
     if (sval > 0.0f) {
       const float y = __frcp_rn(denom);
       if (rcp_div_ok_all(denom)) {
+        // div_rn_by_rcp two elements per packed fp32x2 instruction (same bits)
+        const float2 y2 = make_float2(y, y), nd2 = make_float2(-denom, -denom);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = copysignf(div_rn_by_rcp(f[j], denom, y), f[j]);
+        for (int j = 0; j < 16; j += 2) {
+          const float2 f2 = make_float2(f[j], f[j + 1]);
+          const float2 q0 = mul2(f2, y2);
+          const float2 qq = fma2(fma2(q0, nd2, f2), y2, q0);
+          r[j] = copysignf(qq.x, f[j]);
+          r[j + 1] = copysignf(qq.y, f[j + 1]);
+        }
       } else {  // blocks of tiny magnitude (or a huge divisor): per-element guard
         const bool ok = rcp_div_ok(denom);
 #pragma unroll
