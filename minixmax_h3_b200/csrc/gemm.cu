@@ -134,7 +134,7 @@ struct GemmArgs {
 // A plus 128 of B per SM need half of that per FLOP, and its 4 MMAs per slab
 // take 512 cycles instead of 384, which leaves the single issuing thread room.
 // Two 256-column accumulators would fill TMEM, so an NVFP4 pair has one: the
-// epilogue reads its whole share into registers (192 per thread through
+// epilogue reads its whole share into registers (184 per thread through
 // setmaxnreg) and releases it before computing, and five scale slots let
 // the writers run up to five slabs ahead of the MMAs.
 template <int KIND, int PAIR, int EM = EM_STORE>
@@ -180,12 +180,14 @@ struct Cfg {
 
 // NVFP4 pair register split (setmaxnreg per warpgroup): launched at 128 per
 // thread (512 x 128), the control warpgroup (producer, MMA, two idle warps)
-// drops to 56, the scale writers to 72, and the two epilogue warpgroups rise
-// to 192 so each epilogue thread can hold its 128 accumulator columns.
+// and the scale writers drop to 72, and the two epilogue warpgroups rise to
+// 184 so each epilogue thread can hold its 128 accumulator columns.  (With
+// the control warpgroup at 56 and the epilogue at 192 the issuer's loop
+// spilled: 4-16 % slower on store and gate-residual epilogues.)
 constexpr int PAIR_LAUNCH_REGS = 128;
-constexpr int REGS_CTL = 56;
+constexpr int REGS_CTL = 72;
 constexpr int REGS_SFW = 72;
-constexpr int REGS_EPI = 192;
+constexpr int REGS_EPI = 184;
 static_assert(4 * REGS_CTL + 4 * REGS_SFW + 8 * REGS_EPI <= 16 * PAIR_LAUNCH_REGS, "register split exceeds launch");
 
 // TMEM column of NVFP4 scale slot `slot` (A scales at +4j, B scales at
@@ -402,8 +404,8 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
     // the whole warp runs the loop converged (lane 0 waits and broadcasts the
     // verdict, every lane computes the descriptors, one elected lane issues
     // each slab's MMAs and commit), 3-4 % faster than a lone lane.  NVFP4
-    // keeps the lone lane: its issuer warpgroup runs at 56 registers, where
-    // the converged loop spilled and measured slower.
+    // keeps the lone lane, which measured faster on store and gate-residual
+    // epilogues (the converged loop only on GELU).
     constexpr bool CONV = KIND == KIND_I8;
     auto issuer_wait = [&](uint64_t* bar, uint32_t parity, int site, auto spin, auto cluster_scope) -> bool {
       constexpr bool SP = decltype(spin)::value, CL = decltype(cluster_scope)::value;
