@@ -112,11 +112,12 @@ struct AttnArgs {
   float scale_log2;
 };
 
+// Every lane polls the barrier (one shared state, so one verdict per poll);
+// the vote keeps the warp's view uniform in every case.
 template <bool SPIN = false>
 H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait<SPIN>(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  const bool ok = mbar_wait<SPIN>(bar, parity, &g_status, site, abort_flag);
+  return __all_sync(0xffffffffu, ok);
 }
 
 H3B_DEV float fast_exp2(float x) {
