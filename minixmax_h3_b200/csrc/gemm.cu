@@ -16,7 +16,8 @@
 //               barrier, which only the leader arms (for both CTAs' bytes);
 //               NVFP4 scale bytes land on each CTA's own sf_ready barrier.
 //   warp 1      TMEM allocator; in the leader (the only CTA of a single-CTA
-//               launch) the single-thread MMA issuer.  tcgen05.commit (to
+//               launch) the MMA issuer: the warp polls the barriers
+//               together, one elected lane issues.  tcgen05.commit (to
 //               both CTAs of a pair) releases smem slots and publishes
 //               finished accumulators.
 //   epilogue    8 warps (2-9; 8-15 in an NVFP4 pair) for this CTA's 128
@@ -38,7 +39,7 @@
 //               nothing but MMAs.  (With one single-CTA writer per quadrant,
 //               the ones sharing a scheduler with the producer or the MMA
 //               thread fell a slab behind and paced the pipe.)
-// The single issuing thread is the MMA pipe's feeder: a block-scaled MMA
+// The issuing lane is the MMA pipe's feeder: a block-scaled MMA
 // takes ~55-75 cycles to issue, a commit ~60-75 and a barrier poll ~80, so 4
 // NVFP4 MMAs of 128x192x64 per 384-cycle slab leave it no room for the 12
 // scale copies (tcgen05.cp, ~45 cycles of issue each) a slab would need.
@@ -61,8 +62,6 @@
 // Operands are K-major with the 128-byte swizzle.  No load uses cluster
 // multicast.  Every wait is bounded; both CTAs of a pair stay resident until
 // a final cluster barrier.
-#include <type_traits>
-
 #include "h3b_common.cuh"
 #include "h3b_host.hpp"
 
@@ -132,7 +131,7 @@ struct GemmArgs {
 // FP4 tile at full MMA rate reads ~107 B/clk of operands from shared memory
 // while TMA writes as many, against ~128 B/clk per SM; a pair's 128 rows of
 // A plus 128 of B per SM need half of that per FLOP, and its 4 MMAs per slab
-// take 512 cycles instead of 384, which leaves the single issuing thread room.
+// take 512 cycles instead of 384, which leaves the issuing lane room.
 // Two 256-column accumulators would fill TMEM, so an NVFP4 pair has one: the
 // epilogue reads its whole share into registers (184 per thread through
 // setmaxnreg) and releases it before computing, and five scale slots let
@@ -220,12 +219,13 @@ static_assert(smem_bytes<KIND_I8, 2>() <= 227 * 1024 && smem_bytes<KIND_NVF4, 1>
                   smem_bytes<KIND_NVF4, 2, EM_SEQ2HEAD>() <= 227 * 1024 && smem_bytes<KIND_I8, 2, EM_SEQ2HEAD>() <= 227 * 1024,
               "shared memory budget");
 
-// Lane 0 waits, the verdict is broadcast so the whole warp stays converged.
+// Every lane polls the barrier (one shared state, so one verdict per poll);
+// the vote keeps the warp's view uniform in every case.  (A lane-0 poll
+// with the verdict shuffled to the others cost the attention kernel 5 %.)
 template <bool SPIN = false, bool CLUSTER = false>
 H3B_DEV bool warp_wait(uint64_t* bar, uint32_t parity, int site, volatile int* abort_flag) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait<SPIN, CLUSTER>(bar, parity, &g_status, site, abort_flag) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  const bool ok = mbar_wait<SPIN, CLUSTER>(bar, parity, &g_status, site, abort_flag);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Byte offset of 16-byte chunk c of row r in a 32-row x 64-byte staging
@@ -400,30 +400,12 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // (the leader only under PAIR = 2: its MMAs fill both CTAs' TMEM).  INT8:
-    // the whole warp runs the loop converged (lane 0 waits and broadcasts the
-    // verdict, every lane computes the descriptors, one elected lane issues
-    // each slab's MMAs and commit), 3-4 % faster than a lone lane.  NVFP4
-    // keeps the lone lane, which measured faster on store and gate-residual
-    // epilogues (the converged loop only on GELU).
-    constexpr bool CONV = KIND == KIND_I8;
-    auto issuer_wait = [&](uint64_t* bar, uint32_t parity, int site, auto spin, auto cluster_scope) -> bool {
-      constexpr bool SP = decltype(spin)::value, CL = decltype(cluster_scope)::value;
-      if constexpr (CONV)
-        return warp_wait<SP, CL>(bar, parity, site, abort_flag);
-      else
-        return mbar_wait<SP, CL>(bar, parity, &g_status, site, abort_flag);
-    };
-    auto issuer_one = [&]() -> bool {
-      if constexpr (CONV)
-        return elect_one();
-      else
-        return true;
-    };
-    auto issuer_sync = [&]() {
-      if constexpr (CONV) __syncwarp();
-    };
-    if (leader && (CONV || lane == 0)) {
+    // (the leader only under PAIR = 2: its MMAs fill both CTAs' TMEM).  The
+    // whole warp runs the loop converged: every lane polls the barriers and
+    // computes the descriptors, one elected lane issues each slab's MMAs and
+    // commit.  Against a lone issuing lane: INT8 +3 %, NVFP4 GELU epilogue
+    // +12 %, gate-residual +4 %.
+    if (leader) {
       int it = 0;
       int local = 0;
       // stage, its phase and the scale slot of slab `it`, kept as running
@@ -433,15 +415,14 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters, ++local) {
         const int buf = local % C::NACC;
         const int use = local / C::NACC;
-        if (use > 0 && !issuer_wait(&bars->acc_empty[buf], (use - 1) & 1, 2, std::false_type{},
-                                    std::integral_constant<bool, PAIR == 2>{})) {
+        if (use > 0 && !warp_wait<false, PAIR == 2>(&bars->acc_empty[buf], (use - 1) & 1, 2, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * C::ACC_STRIDE;
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          if (!issuer_wait(&bars->full[s], static_cast<uint32_t>(ph), 3, std::true_type{}, std::false_type{})) {
+          if (!warp_wait<true>(&bars->full[s], static_cast<uint32_t>(ph), 3, abort_flag)) {
             ok = false;
             break;
           }
@@ -449,7 +430,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
           tc_fence_after();
           const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(sA + s * A_BYTES));
           const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(sB + s * C::B_BYTES));
-          if (issuer_one()) {
+          if (elect_one()) {
             if constexpr (KIND == KIND_I8) {
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -477,7 +458,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
             else
               tc_commit(&bars->empty[s]);
           }
-          issuer_sync();
+          __syncwarp();
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
@@ -485,26 +466,23 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
           if (++slot == C::SF_SLOTS) slot = 0;
         }
         if (!ok) break;
-        if (issuer_one()) {
+        if (elect_one()) {
           if constexpr (PAIR == 2)  // accumulator complete in both CTAs
             tc_commit_pair_mc(&bars->acc_full[buf], 0x3);
           else
             tc_commit(&bars->acc_full[buf]);
         }
-        issuer_sync();
+        __syncwarp();
       }
       // Drain all MMAs this warp issued before TMEM is released.
-      if (issuer_one()) {
+      if (elect_one()) {
         if constexpr (PAIR == 2)
           tc_commit_pair(&bars->drain);
         else
           tc_commit(&bars->drain);
       }
-      issuer_sync();
-      if constexpr (CONV)
-        warp_wait(&bars->drain, 0, 8, nullptr);
-      else
-        mbar_wait(&bars->drain, 0, &g_status, 8, nullptr);
+      __syncwarp();
+      warp_wait(&bars->drain, 0, 8, nullptr);
     }
   }
   } else if (KIND == KIND_NVF4 && warp >= C::SF_WARP0 && warp < C::SF_WARP0 + C::SF_WARPS) {
