@@ -420,7 +420,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < n_kv; ++j) {
       // s_full[wg] completes once per tile; the MMA cannot publish S(j+1)
       // before P(j) is written below, so this wait is one phase behind.
-      if (!warp_wait(&bars->s_full[wg], j & 1, 20, abort_flag)) {
+      // (polled without a suspend hint: +0.8 % against a hinted wait)
+      if (!warp_wait<true>(&bars->s_full[wg], j & 1, 20, abort_flag)) {
         ok = false;
         break;
       }

@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(Cfg<KIND, PAIR, EM>::THREADS, 1)
     for (int tile = cluster; tile < num_tiles; tile += n_clusters, ++local) {
       const int buf = local % C::NACC;
       const int use = local / C::NACC;
-      if (!warp_wait(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
+      if (!warp_wait<true>(&bars->acc_full[buf], use & 1, 4, abort_flag)) break;
       tc_fence_after();
       const int m0 = ((tile / n_tiles) * PAIR + static_cast<int>(rank)) * BM;
       const int n0 = (tile % n_tiles) * BN;
