@@ -10,7 +10,8 @@
 //   warps 4-7   softmax for Q1
 //   warp 8      TMA producer: Q0/Q1 once, K through a 2-deep ring, V through
 //               a 3-deep ring (one release wait per K/V tile covers both)
-//   warp 9      TMEM allocator + single-thread MMA issuer
+//   warp 9      TMEM allocator + MMA issuer (the warp polls together, one
+//               elected lane issues)
 //   warps 10-11 idle (complete the third warpgroup for setmaxnreg)
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each.  The softmax
 // writes P as packed bf16 into the first 64 columns of the S region it read,
@@ -315,11 +316,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs the schedule converged: lane 0 waits (polling
-    // without a suspend hint: this is the latency-critical hand-off from the
-    // softmax back to the tensor pipe) and broadcasts the verdict, every lane
-    // computes the descriptors, and one elected lane issues each batch of
-    // tcgen05.mma and its commit.
+    // The whole warp runs the schedule converged: every lane polls each
+    // barrier (without a suspend hint: this is the latency-critical hand-off
+    // from the softmax back to the tensor pipe) and the verdict is a vote,
+    // every lane computes the descriptors, and one elected lane issues each
+    // batch of tcgen05.mma and its commit.
     bool ok = warp_wait<true>(&bars->q_full, 0, 3, abort_flag);
     tc_fence_after();
     // k_full[j % 2] completes once per use of the slot; its next phase is
